@@ -1,0 +1,300 @@
+"""ctypes binding of the native library ``libascan_b200.so`` (C ABI: include/ascan.h).
+
+Every op of this package reaches the GPU through the three entry points bound
+here -- ``ascan_forward``, ``ascan_backward`` and ``ascan_shift_pad`` -- with
+raw device pointers, sizes and torch's current CUDA stream.  There is no CPU
+path: a missing library, a CPU tensor or a machine without CUDA raises.
+
+Device-side checks (malformed ``cu_seqlens``, a look-back that gave up) set a
+sticky error word on the device.  Reading it needs a device synchronisation,
+so it is only read when sync checking is on (``set_sync_check(True)`` or the
+environment variable ``ASCAN_SYNC_CHECK=1``) or when :func:`check_device_error`
+is called.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import warnings
+from pathlib import Path
+
+import torch
+
+LIB_NAME = "libascan_b200.so"
+LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
+
+ASCAN_OK = 0
+DEV_ERR_CU_END = 0x1
+DEV_ERR_CU_ORDER = 0x2
+DEV_ERR_LOOKBACK = 0x4
+
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+INDEX_CODES = {torch.int32: 0, torch.int64: 1}
+
+# Symbols declared in include/ascan.h.
+EXPORTED_SYMBOLS = (
+  "ascan_abi_version",
+  "ascan_build_info",
+  "ascan_strerror",
+  "ascan_workspace_size",
+  "ascan_forward",
+  "ascan_backward",
+  "ascan_shift_pad",
+  "ascan_get_device_error",
+  "ascan_clear_device_error",
+)
+
+
+class ScanError(RuntimeError):
+  """An error reported by the native library or detected on the device."""
+
+
+_lib = None
+_load_error: Exception | None = None
+_sync_check = os.environ.get("ASCAN_SYNC_CHECK", "0") not in ("", "0")
+
+
+def _bind(lib) -> None:
+  p, i64, ci, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+  lib.ascan_abi_version.restype = ci
+  lib.ascan_abi_version.argtypes = []
+  lib.ascan_build_info.restype = ctypes.c_char_p
+  lib.ascan_build_info.argtypes = []
+  lib.ascan_strerror.restype = ctypes.c_char_p
+  lib.ascan_strerror.argtypes = [ci]
+  lib.ascan_workspace_size.restype = sz
+  lib.ascan_workspace_size.argtypes = [i64, i64, ci]
+  lib.ascan_forward.restype = ci
+  lib.ascan_forward.argtypes = [p, p, p, p, p, ci, i64, i64, i64, ci, ci, p, sz, p]
+  lib.ascan_backward.restype = ci
+  lib.ascan_backward.argtypes = [p, p, p, p, p, p, ci, i64, i64, i64, ci, ci, p, sz, p]
+  lib.ascan_shift_pad.restype = ci
+  lib.ascan_shift_pad.argtypes = [p, p, p, ci, i64, i64, i64, ci, ctypes.c_double, ci, ci, p]
+  lib.ascan_get_device_error.restype = ci
+  lib.ascan_get_device_error.argtypes = [ci, ctypes.POINTER(ctypes.c_uint),
+                                         ctypes.POINTER(ctypes.c_longlong)]
+  lib.ascan_clear_device_error.restype = ci
+  lib.ascan_clear_device_error.argtypes = [ci]
+
+
+def load(path: str | os.PathLike | None = None):
+  """Load (once) and return the native library; raise if it is missing."""
+  global _lib, _load_error
+  if _lib is not None:
+    return _lib
+  target = Path(path) if path is not None else LIB_PATH
+  if not target.exists():
+    _load_error = ScanError(
+      f"native library {target} is missing; build it with "
+      "`python -m associative_scan_triton._build` (needs nvcc)")
+    raise _load_error
+  lib = ctypes.CDLL(str(target))
+  _bind(lib)
+  _lib = lib
+  _load_error = None
+  return lib
+
+
+def try_load() -> bool:
+  """Load the library if it exists; warn (do not raise) when it does not."""
+  try:
+    load()
+    return True
+  except ScanError as e:  # surfaced again, as an exception, by the first op
+    warnings.warn(str(e), RuntimeWarning, stacklevel=2)
+    return False
+
+
+def library_path() -> Path:
+  return LIB_PATH
+
+
+def set_sync_check(enabled: bool) -> None:
+  """Synchronise after every op and raise on a device-side error."""
+  global _sync_check
+  _sync_check = bool(enabled)
+
+
+def sync_check_enabled() -> bool:
+  return _sync_check
+
+
+def strerror(status: int) -> str:
+  return load().ascan_strerror(int(status)).decode()
+
+
+def describe_device_error(code: int) -> str:
+  parts = []
+  if code & DEV_ERR_CU_END:
+    parts.append("cu_seqlens[-1] does not equal the packed length of the tensors")
+  if code & DEV_ERR_CU_ORDER:
+    parts.append("cu_seqlens is not monotone or lies outside [0, packed length]")
+  if code & DEV_ERR_LOOKBACK:
+    parts.append("a tile's predecessor did not publish within the bounded wait")
+  return "; ".join(parts) or f"device error {code:#x}"
+
+
+def get_device_error(device: int | torch.device | None = None) -> tuple[int, int]:
+  """Synchronise ``device`` and return its sticky (error bits, detail)."""
+  dev = _device_index(device)
+  code, detail = ctypes.c_uint(0), ctypes.c_longlong(0)
+  rc = load().ascan_get_device_error(dev, ctypes.byref(code), ctypes.byref(detail))
+  if rc != ASCAN_OK:
+    raise ScanError(f"ascan_get_device_error: {strerror(rc)}")
+  return int(code.value), int(detail.value)
+
+
+def clear_device_error(device: int | torch.device | None = None) -> None:
+  rc = load().ascan_clear_device_error(_device_index(device))
+  if rc != ASCAN_OK:
+    raise ScanError(f"ascan_clear_device_error: {strerror(rc)}")
+
+
+def check_device_error(device: int | torch.device | None = None) -> None:
+  """Raise (and clear) if a kernel on ``device`` reported an error."""
+  code, detail = get_device_error(device)
+  if code:
+    clear_device_error(device)
+    raise ScanError(f"device-side error: {describe_device_error(code)} (detail {detail})")
+
+
+def _device_index(device) -> int:
+  if device is None:
+    return torch.cuda.current_device()
+  if isinstance(device, torch.device):
+    return device.index if device.index is not None else torch.cuda.current_device()
+  return int(device)
+
+
+# ---------------------------------------------------------------------------
+# argument checking
+# ---------------------------------------------------------------------------
+
+
+def _require_cuda(name: str, t: torch.Tensor, device: torch.device | None) -> None:
+  if not isinstance(t, torch.Tensor):
+    raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
+  if t.device.type != "cuda":
+    raise ValueError(
+      f"{name} is on {t.device}; associative_scan_triton (B200) runs on CUDA tensors only")
+  if device is not None and t.device != device:
+    raise ValueError(f"{name} is on {t.device}, expected {device}")
+
+
+def _layout(t: torch.Tensor, num_channels: int) -> tuple[int, int]:
+  """(C, BL) of a packed tensor given the channel count of the launch grid."""
+  if num_channels <= 0:
+    raise ValueError(f"number of channels must be positive, got {num_channels}")
+  if t.dim() == 2:
+    if num_channels > t.shape[0]:
+      raise ValueError(f"grid asks for {num_channels} channels, tensor has {t.shape[0]}")
+    return int(num_channels), int(t.shape[1])
+  if t.numel() % num_channels:
+    raise ValueError(f"{t.numel()} elements are not {num_channels} equal channels")
+  return int(num_channels), int(t.numel() // num_channels)
+
+
+def _workspace(n_channels: int, seq_total: int, dtype_code: int, device) -> torch.Tensor:
+  nbytes = int(load().ascan_workspace_size(n_channels, seq_total, dtype_code))
+  return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def _stream_ptr(device: torch.device) -> int:
+  return torch.cuda.current_stream(device).cuda_stream
+
+
+def _finish(rc: int, what: str, device: torch.device) -> None:
+  if rc != ASCAN_OK:
+    raise ScanError(f"{what}: {strerror(rc)}")
+  if _sync_check:
+    check_device_error(device)
+
+
+def _check_inputs(names_tensors, cu_seqlens, num_seq):
+  first = names_tensors[0][1]
+  device = first.device
+  for name, t in names_tensors:
+    _require_cuda(name, t, device if name != names_tensors[0][0] else None)
+    if not t.is_contiguous():
+      raise ValueError(f"{name} must be contiguous")
+    if t.dtype != first.dtype:
+      raise TypeError(f"{name} has dtype {t.dtype}, expected {first.dtype}")
+  if first.dtype not in DTYPE_CODES:
+    raise TypeError(f"unsupported dtype {first.dtype}; use float32, float16 or bfloat16")
+  _require_cuda("cu_seqlens", cu_seqlens, device)
+  if cu_seqlens.dtype not in INDEX_CODES:
+    raise TypeError(f"cu_seqlens must be int32 or int64, got {cu_seqlens.dtype}")
+  if not cu_seqlens.is_contiguous():
+    raise ValueError("cu_seqlens must be contiguous")
+  if cu_seqlens.numel() != num_seq + 1:
+    raise ValueError(f"cu_seqlens has {cu_seqlens.numel()} entries, expected {num_seq + 1}")
+  return device
+
+
+# ---------------------------------------------------------------------------
+# the three native entry points
+# ---------------------------------------------------------------------------
+
+
+def forward(gates: torch.Tensor, tokens: torch.Tensor, tokens_out: torch.Tensor,
+            gates_out: torch.Tensor | None, cu_seqlens: torch.Tensor, num_seq: int,
+            num_channels: int, reverse: bool) -> None:
+  """ascan_forward on torch tensors (tokens_out may be tokens; gates_out may be gates)."""
+  tensors = [("gates", gates), ("tokens", tokens), ("tokens_out", tokens_out)]
+  if gates_out is not None:
+    tensors.append(("gates_out", gates_out))
+  device = _check_inputs(tensors, cu_seqlens, num_seq)
+  C, BL = _layout(tokens, num_channels)
+  for name, t in tensors:
+    if _layout(t, num_channels) != (C, BL):
+      raise ValueError(f"{name} shape {tuple(t.shape)} does not match tokens {tuple(tokens.shape)}")
+  lib = load()
+  dcode = DTYPE_CODES[tokens.dtype]
+  with torch.cuda.device(device):
+    ws = _workspace(C, BL, dcode, device)
+    rc = lib.ascan_forward(
+      gates.data_ptr(), tokens.data_ptr(), tokens_out.data_ptr(),
+      gates_out.data_ptr() if gates_out is not None else None,
+      cu_seqlens.data_ptr(), INDEX_CODES[cu_seqlens.dtype], int(num_seq), C, BL, dcode,
+      int(bool(reverse)), ws.data_ptr(), ws.numel(), _stream_ptr(device))
+  _finish(rc, "ascan_forward", device)
+
+
+def backward(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
+             d_tokens: torch.Tensor, d_gates: torch.Tensor, cu_seqlens: torch.Tensor,
+             num_seq: int, num_channels: int, causal: bool) -> None:
+  """ascan_backward on torch tensors."""
+  tensors = [("grad", grad), ("gates", gates), ("states", states), ("d_tokens", d_tokens),
+             ("d_gates", d_gates)]
+  device = _check_inputs(tensors, cu_seqlens, num_seq)
+  C, BL = _layout(grad, num_channels)
+  for name, t in tensors:
+    if _layout(t, num_channels) != (C, BL):
+      raise ValueError(f"{name} shape {tuple(t.shape)} does not match grad {tuple(grad.shape)}")
+  lib = load()
+  dcode = DTYPE_CODES[grad.dtype]
+  with torch.cuda.device(device):
+    ws = _workspace(C, BL, dcode, device)
+    rc = lib.ascan_backward(
+      grad.data_ptr(), gates.data_ptr(), states.data_ptr(), d_tokens.data_ptr(),
+      d_gates.data_ptr(), cu_seqlens.data_ptr(), INDEX_CODES[cu_seqlens.dtype], int(num_seq),
+      C, BL, dcode, int(bool(causal)), ws.data_ptr(), ws.numel(), _stream_ptr(device))
+  _finish(rc, "ascan_backward", device)
+
+
+def shift_pad(data: torch.Tensor, out: torch.Tensor, cu_seqlens: torch.Tensor,
+              pad_value: float, backward: bool, wrap: bool) -> None:
+  """ascan_shift_pad on a 2-D [C, BL] tensor."""
+  if data.dim() != 2:
+    raise ValueError(f"shift_pad expects a [C, BL] tensor, got shape {tuple(data.shape)}")
+  num_seq = cu_seqlens.numel() - 1
+  device = _check_inputs([("data", data), ("out", out)], cu_seqlens, num_seq)
+  C, BL = int(data.shape[0]), int(data.shape[1])
+  lib = load()
+  with torch.cuda.device(device):
+    rc = lib.ascan_shift_pad(
+      data.data_ptr(), out.data_ptr(), cu_seqlens.data_ptr(), INDEX_CODES[cu_seqlens.dtype],
+      num_seq, C, BL, DTYPE_CODES[data.dtype], float(pad_value), int(bool(backward)),
+      int(bool(wrap)), _stream_ptr(device))
+  _finish(rc, "ascan_shift_pad", device)

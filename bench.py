@@ -1,0 +1,487 @@
+"""Benchmark of the packed-varlen linear scan on B200 (one JSON line on stdout).
+
+Workload (the headline configuration of the reference's kernel benchmark,
+reference bench/bench_kernels.py:42-79 and its B=8, C=1536 tables): causal
+fwd+bwd over B=8 packed sequences of T=4096, C=1536 channels, float32,
+gates ~ U(0.9, 1), tokens ~ N(0, 1), upstream gradient ~ N(0, 1), seeded
+synthetic data.  One step = one forward kernel + one fused backward kernel over
+the whole batch.  Metric: achieved HBM GB/s of algorithmic traffic
+(fwd 3 x 4 B + bwd 5 x 4 B = 32 B per element), plus ms per step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank runs the same workload on its own GPU (its own
+channel block, no collective on the data path: weak scaling); the timed region
+is bracketed by barriers and the slowest rank's time is reported.
+
+``--impl reference`` times the reference's CPU algorithm -- the fp64 sequential
+scan of its tests (oracle/ascan_oracle.c restates it) -- on the host cores with
+every available thread, on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "associative-scan-triton_b200"))
+sys.path.insert(0, str(REPO))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "fwd & fwd+bwd ms and achieved HBM GB/s at B=8,C=1536,T=128..65536"
+B, T, C = 8, 4096, 1536
+FWD_BYTES_PER_ELEM = 3 * 4    # read g, x; write y (fp32)
+BWD_BYTES_PER_ELEM = 5 * 4    # read dy, g, h; write dx, dg
+STEP_BYTES_PER_ELEM = FWD_BYTES_PER_ELEM + BWD_BYTES_PER_ELEM
+L2_BYTES = 126 * 2**20
+PROFILE_SUMMARY = REPO / "profiles" / "scan_bwd_kernel_config2.md"
+
+
+def _peaks() -> tuple[float, str]:
+  p = REPO / "MEASURED_PEAKS.json"
+  try:
+    return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+  except Exception:
+    return 6650.0, "fallback"
+
+
+def _profile_traffic() -> float | None:
+  """DRAM bytes per bwd launch from the committed ncu summary, if present."""
+  try:
+    for line in PROFILE_SUMMARY.read_text().splitlines():
+      if line.startswith("traffic_bytes_per_launch_config2:"):
+        return float(line.split(":", 1)[1].strip())
+  except OSError:
+    pass
+  return None
+
+
+class ClockSampler:
+  """nvidia-smi clock / throttle-reason sampling while the GPU is busy."""
+
+  FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+            "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+            "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+  def __init__(self, device_index: int):
+    self.proc = None
+    self.path = None
+    try:
+      uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+      self.gpu = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+    except Exception:
+      self.gpu = None
+
+  def start(self):
+    if self.gpu is None:
+      return self
+    import tempfile
+    fd, self.path = tempfile.mkstemp(prefix="ascan_clocks_", suffix=".csv")
+    os.close(fd)
+    try:
+      self.proc = subprocess.Popen(
+        ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
+         "--format=csv,noheader,nounits", "-lms", "50"],
+        stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+    except OSError:
+      self.proc = None
+    return self
+
+  def stop(self) -> dict:
+    if self.proc is None:
+      return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    self.proc.terminate()
+    try:
+      self.proc.wait(timeout=5)
+    except subprocess.TimeoutExpired:
+      self.proc.kill()
+    rows = []
+    for line in Path(self.path).read_text().splitlines():
+      parts = [p.strip() for p in line.split(",")]
+      if len(parts) == 8:
+        rows.append(parts)
+    os.unlink(self.path)
+    if not rows:
+      return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+    mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+    pw = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+    names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+    loaded = sorted(sm)[len(sm) // 2:] if sm else []  # upper half = under load
+    return {"sm_mhz": statistics.median(loaded) if loaded else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "power_w_max": max(pw) if pw else None,
+            "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+
+def _dist_setup(n_gpus: int):
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  if world > 1:
+    import torch.distributed as dist
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    return dist, dist.get_rank(), world, local
+  return None, 0, 1, 0
+
+
+def _barrier(dist, device):
+  if dist is not None:
+    dist.barrier(device_ids=[device.index])
+
+
+def _max_over_ranks(dist, value: float, device) -> float:
+  if dist is None:
+    return value
+  t = torch.tensor([value], dtype=torch.float64, device=device)
+  dist.all_reduce(t, op=dist.ReduceOp.MAX)
+  return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+
+def _make_workload(device, seed, C_=C, B_=B, T_=T, dtype=torch.float32):
+  gen = torch.Generator(device=device).manual_seed(seed)
+  BL = B_ * T_
+  g = (0.9 + 0.1 * torch.rand(C_, BL, device=device, generator=gen)).to(dtype)
+  x = torch.randn(C_, BL, device=device, generator=gen).to(dtype)
+  dy = torch.randn(C_, BL, device=device, generator=gen).to(dtype)
+  cu = torch.arange(B_ + 1, device=device, dtype=torch.int32) * T_
+  return g, x, dy, cu
+
+
+def _sweep(ast, device) -> list[dict]:
+  """fwd and fwd+bwd at B=8, C=1536, T=128..65536 (fp32), L2 flushed when inputs fit in it."""
+  out = []
+  flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
+  for Tn in [2**i for i in range(7, 17)]:
+    g, x, dy, cu = _make_workload(device, 100 + Tn, T_=Tn)
+    y, dx, dg = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+    grid = (B, 1, C)
+    n = C * B * Tn
+    small = 3 * n * 4 < L2_BYTES * 2
+
+    def fwd():
+      ast.forward_scan_full(g, x, cu, grid, REVERSE=False, CHUNK_SIZE=512, TESTING=False,
+                            tokens_out=y)
+
+    def bwd():
+      ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, grid, CHUNK_SIZE=512, CAUSAL=True)
+
+    reps = 30 if Tn <= 8192 else 10
+    res = {}
+    for name, fns in (("fwd", (fwd,)), ("fwdbwd", (fwd, bwd))):
+      for _ in range(3):
+        for f in fns:
+          f()
+      times = []
+      for _ in range(reps):
+        if small:
+          flush.fill_(1.0)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for f in fns:
+          f()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+      ms = statistics.median(times)
+      bpe = FWD_BYTES_PER_ELEM if name == "fwd" else STEP_BYTES_PER_ELEM
+      res[f"{name}_ms"] = round(ms, 5)
+      res[f"{name}_gbs"] = round(bpe * n / (ms * 1e-3) / 1e9, 1)
+    out.append({"T": Tn, **res})
+    del g, x, dy, y, dx, dg
+    torch.cuda.empty_cache()
+  return out
+
+
+def _e2e(ast, device, g_dev, x_dev, dy_dev, cu, steps: int) -> dict:
+  """scan_causal fwd+bwd through the public API with host buffers every step."""
+  pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+  g_h, x_h, dy_h = pin(g_dev), pin(x_dev), pin(dy_dev)
+  y_h = torch.empty_like(g_h).pin_memory()
+  dg_h = torch.empty_like(g_h).pin_memory()
+  dx_h = torch.empty_like(g_h).pin_memory()
+  g_b, x_b, dy_b = torch.empty_like(g_dev), torch.empty_like(x_dev), torch.empty_like(dy_dev)
+  args = {"cu_seqlens": cu, "chunk_size": 512, "grid": ast.get_grid(len(cu), T, 512, C)}
+
+  def step():
+    g_b.copy_(g_h, non_blocking=True)
+    x_b.copy_(x_h, non_blocking=True)
+    dy_b.copy_(dy_h, non_blocking=True)
+    g_l = g_b.detach().requires_grad_(True)
+    x_l = x_b.detach().requires_grad_(True)
+    y = ast.scan_causal(g_l, x_l, args)
+    y.backward(dy_b)
+    y_h.copy_(y.detach(), non_blocking=True)
+    dg_h.copy_(g_l.grad, non_blocking=True)
+    dx_h.copy_(x_l.grad, non_blocking=True)
+
+  for _ in range(2):
+    step()
+  torch.cuda.synchronize()
+  s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  s.record()
+  for _ in range(steps):
+    step()
+  e.record()
+  e.synchronize()
+  ms = s.elapsed_time(e) / steps
+  n = g_dev.numel()
+  return {"ms_per_step": ms, "steps": steps, "h2d_bytes_per_step": 3 * n * 4,
+          "d2h_bytes_per_step": 3 * n * 4, "n": n}
+
+
+def _cpu_baseline(seconds: float = 10.0) -> dict:
+  """The reference's CPU algorithm (fp64 sequential scan, oracle port) on a channel sample."""
+  from oracle import oracle
+  threads = oracle.num_threads()
+  c_sample = max(64, 4 * threads)
+  rng = np.random.default_rng(0)
+  BL = B * T
+  g = rng.uniform(0.9, 1.0, size=(c_sample, BL)).astype(np.float32)
+  x = rng.standard_normal((c_sample, BL), dtype=np.float32)
+  dy = rng.standard_normal((c_sample, BL), dtype=np.float32)
+  cu = np.arange(B + 1, dtype=np.int64) * T
+  oracle.scan_fwd_bwd(g[:threads], x[:threads], dy[:threads], cu)  # warm
+  t0 = time.perf_counter()
+  passes = 0
+  while True:
+    oracle.scan_fwd_bwd(g, x, dy, cu)
+    passes += 1
+    if time.perf_counter() - t0 >= seconds:
+      break
+  dt = time.perf_counter() - t0
+  elems = passes * c_sample * BL
+  return {"value": round(STEP_BYTES_PER_ELEM * elems / dt / 1e9, 3), "unit": "GB/s",
+          "cores": threads, "kind": "port",
+          "sample": (f"{passes} fwd+bwd passes over {c_sample} of {C} channels x B*T={BL} "
+                     f"(fp32 in, fp64 sequential, OpenMP over channels), {dt:.1f} s; "
+                     f"same 32 B/elem accounting"),
+          "ms_per_full_step_equiv": round(dt / elems * C * BL * 1e3, 1)}
+
+
+def run_ours(args) -> dict | None:
+  dist, rank, world, local = _dist_setup(args.gpus)
+  device = torch.device("cuda", local)
+  torch.cuda.set_device(device)
+  import associative_scan_triton as ast
+  from associative_scan_triton import _lib
+  _lib.load()
+  _lib.set_sync_check(False)
+
+  g, x, dy, cu = _make_workload(device, seed=1234 + rank)
+  y, dx, dg = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+  grid = (B, 1, C)
+  n = C * B * T
+
+  def fwd():
+    ast.forward_scan_full(g, x, cu, grid, REVERSE=False, CHUNK_SIZE=512, TESTING=False,
+                          tokens_out=y)
+
+  def bwd():
+    ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, grid, CHUNK_SIZE=512, CAUSAL=True)
+
+  sampler = ClockSampler(local).start() if rank == 0 else None
+  for _ in range(args.warmup):
+    fwd()
+    bwd()
+  torch.cuda.synchronize()
+  _lib.check_device_error(device)
+
+  ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+  _barrier(dist, device)
+  torch.cuda.synchronize()
+  start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  start.record()
+  for i in range(args.steps):
+    ev[i][0].record()
+    fwd()
+    ev[i][1].record()
+    bwd()
+    ev[i][2].record()
+  stop.record()
+  torch.cuda.synchronize()
+  _barrier(dist, device)
+  total_ms = start.elapsed_time(stop)
+  fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+  bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+  total_ms = _max_over_ranks(dist, total_ms, device)
+  fwd_ms = _max_over_ranks(dist, fwd_ms, device)
+  bwd_ms = _max_over_ranks(dist, bwd_ms, device)
+  _lib.check_device_error(device)
+  clocks = sampler.stop() if sampler else None
+
+  ms_per_step = total_ms / args.steps
+  value = STEP_BYTES_PER_ELEM * n * world / (ms_per_step * 1e-3) / 1e9
+
+  e2e_steps = max(3, min(args.steps, 10))
+  e2e = _e2e(ast, device, g, x, dy, cu, e2e_steps)
+  e2e_ms = _max_over_ranks(dist, e2e["ms_per_step"], device)
+
+  if dist is not None:
+    _barrier(dist, device)
+    dist.destroy_process_group()
+  if rank != 0:
+    return None
+
+  peak, peak_kind = _peaks()
+  bwd_achieved = BWD_BYTES_PER_ELEM * n / (bwd_ms * 1e-3) / 1e9
+  fwd_achieved = FWD_BYTES_PER_ELEM * n / (fwd_ms * 1e-3) / 1e9
+  traffic = _profile_traffic()
+  line = {
+    "metric": METRIC,
+    "value": round(value, 1),
+    "unit": "GB/s",
+    "n_gpus": world,
+    "steps": args.steps,
+    "warmup": args.warmup,
+    "ms_per_step": round(ms_per_step, 5),
+    "higher_is_better": True,
+    "scaling": "weak",
+    "vs_baseline": None,
+    "dtype": "f32",
+    "data": "synthetic (seeded; gates U(0.9,1), tokens N(0,1), dy N(0,1))",
+    "config": {
+      "workload": f"causal fwd+bwd, B={B} packed x T={T}, C={C}, fp32 (configs[1])",
+      "elements_per_gpu": n, "bytes_per_element_fwd_bwd": STEP_BYTES_PER_ELEM,
+      "api": "forward_scan_full + backward_scan_fused_full -> C ABI",
+      "l2": "inputs larger than L2 (201 MB per tensor vs 126 MB); no flush",
+      "parallelism": f"channel-block replicas x{world}, no collective on the data path",
+    },
+    "fwd_ms": round(fwd_ms, 5),
+    "fwd_gbs": round(fwd_achieved, 1),
+    "bwd_ms": round(bwd_ms, 5),
+    "roofline": {
+      "bound": "hbm", "kernel": "scan_bwd_kernel (fused backward)",
+      "achieved": round(bwd_achieved, 1), "peak": peak, "unit": "GB/s",
+      "frac": round(bwd_achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
+      "traffic": traffic,
+      "algorithmic_bytes_per_launch": BWD_BYTES_PER_ELEM * n,
+      "fwd_frac": round(fwd_achieved / peak, 4),
+      "frac_of_8000_nominal": round(bwd_achieved / 8000.0, 4),
+    },
+    "e2e": {
+      "value": round(STEP_BYTES_PER_ELEM * n * world / (e2e_ms * 1e-3) / 1e9, 2),
+      "unit": "GB/s", "ms_per_step": round(e2e_ms, 3), "steps": e2e["steps"],
+      "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
+      "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
+      "api": "scan_causal(g, x, args) + y.backward(dy), pinned host buffers",
+    },
+    "gpu_launches": 2 * args.steps,
+    "clocks": clocks,
+  }
+  if not args.no_sweep and world == 1:
+    line["sweep_B8_C1536_fp32"] = _sweep(ast, device)
+  if not args.no_cpu_baseline and world == 1:
+    line["cpu_baseline"] = _cpu_baseline(args.cpu_seconds)
+  return line
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's CPU algorithm (oracle port) on host cores
+# ---------------------------------------------------------------------------
+
+
+def run_reference(args) -> dict | None:
+  rank = int(os.environ.get("RANK", "0"))
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  if rank != 0:
+    return None
+  from oracle import oracle
+  threads = oracle.num_threads()
+  BL = B * T
+  cu = np.arange(B + 1, dtype=np.int64) * T
+  rng = np.random.default_rng(0)
+  budget_s = 90.0
+  # size one step's channel sample so that warmup + steps fit the budget
+  probe_c = max(threads, 8)
+  g = rng.uniform(0.9, 1.0, size=(probe_c, BL)).astype(np.float32)
+  x = rng.standard_normal((probe_c, BL), dtype=np.float32)
+  dy = rng.standard_normal((probe_c, BL), dtype=np.float32)
+  t0 = time.perf_counter()
+  oracle.scan_fwd_bwd(g, x, dy, cu)
+  per_chan = (time.perf_counter() - t0) / probe_c
+  per_step_s = min(2.0, budget_s / max(1, args.steps + args.warmup))
+  c_sample = int(max(threads, min(C, per_step_s / max(per_chan, 1e-9))))
+  c_sample = max(1, (c_sample // threads) * threads) if c_sample >= threads else c_sample
+  g = rng.uniform(0.9, 1.0, size=(c_sample, BL)).astype(np.float32)
+  x = rng.standard_normal((c_sample, BL), dtype=np.float32)
+  dy = rng.standard_normal((c_sample, BL), dtype=np.float32)
+  for _ in range(args.warmup):
+    oracle.scan_fwd_bwd(g, x, dy, cu)
+  t0 = time.perf_counter()
+  for _ in range(args.steps):
+    oracle.scan_fwd_bwd(g, x, dy, cu)
+  dt = time.perf_counter() - t0
+  ms_per_step = dt / args.steps * 1e3
+  elems = c_sample * BL
+  value = STEP_BYTES_PER_ELEM * elems / (ms_per_step * 1e-3) / 1e9
+  sample = (f"each step: causal fwd+bwd over {c_sample} of {C} channels x B*T={BL} "
+            f"(fp32 in, fp64 sequential scan, OpenMP over channels)")
+  return {
+    "impl": "reference",
+    "metric": METRIC,
+    "value": round(value, 3),
+    "unit": "GB/s",
+    "n_gpus": world,
+    "steps": args.steps,
+    "warmup": args.warmup,
+    "ms_per_step": round(ms_per_step, 3),
+    "higher_is_better": True,
+    "scaling": "weak",
+    "vs_baseline": None,
+    "dtype": "f64",
+    "data": "synthetic (seeded; gates U(0.9,1), tokens N(0,1), dy N(0,1))",
+    "config": {
+      "workload": f"causal fwd+bwd, B={B} packed x T={T}, C={C}, fp32 (configs[1])",
+      "sampled_channels": c_sample,
+      "implementation": "reference CPU algorithm (sequential_scan_gold + hand-derived backward), "
+                        "restated in C (oracle/ascan_oracle.c)",
+    },
+    "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                     "sample": sample},
+    "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+            "d2h_bytes_per_step": 0},
+  }
+
+
+def main(argv=None) -> int:
+  ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+  ap.add_argument("--gpus", type=int, default=1)
+  ap.add_argument("--steps", type=int, default=400)
+  ap.add_argument("--warmup", type=int, default=20)
+  ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+  ap.add_argument("--no-sweep", action="store_true")
+  ap.add_argument("--no-cpu-baseline", action="store_true")
+  ap.add_argument("--cpu-seconds", type=float, default=10.0)
+  args = ap.parse_args(argv)
+  args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
+  line = run_reference(args) if args.impl == "reference" else run_ours(args)
+  if line is not None:
+    print(json.dumps(line), flush=True)
+  return 0
+
+
+if __name__ == "__main__":
+  sys.exit(main())

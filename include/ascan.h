@@ -1,0 +1,150 @@
+/*
+ * ascan.h -- C ABI of the B200 (sm_100a) first-order linear-recurrence scan.
+ *
+ *   h[t] = g[t] * h[t-1] + x[t]        (causal; reverse: h[t+1] on the right)
+ *
+ * over the packed varlen layout of the reference project: every tensor is
+ * [C, BL] row-major and contiguous, sequence i of channel c occupies
+ * [c*BL + cu[i], c*BL + cu[i+1]), and BL == cu[num_seq]
+ * (reference src/associative_scan_triton/scan_eager.py:74-83,
+ * _kernels.py:49-52).
+ *
+ * Conventions shared by every entry point
+ *   - All data pointers are caller-owned DEVICE memory on the current device.
+ *   - dtype is one of ASCAN_F32 / ASCAN_F16 / ASCAN_BF16; every floating-point
+ *     tensor of one call has that dtype.  Arithmetic is float32 for all three.
+ *   - cu_seqlens is int32 (ASCAN_I32) or int64 (ASCAN_I64) with num_seq + 1
+ *     entries, monotone, cu[num_seq] == seq_total.  Positions of a row before
+ *     cu[0] belong to no sequence and are not written.
+ *   - stream is a cudaStream_t passed as void*; work is enqueued on it and
+ *     the call does not synchronise.
+ *   - workspace: scratch of at least ascan_workspace_size(...) bytes, 256-byte
+ *     aligned, used by one call at a time (two calls in flight at once need two
+ *     workspaces).  Its contents need no initialisation.
+ *   - Return value: ASCAN_OK (0) or a negative ASCAN_E* code describing a bad
+ *     argument or a CUDA launch failure.  Problems only visible on the device
+ *     (a cu_seqlens that is not monotone or does not end at seq_total, a tile
+ *     whose predecessor never published) set a sticky per-device error word
+ *     read by ascan_get_device_error().  No device-side condition can make a
+ *     kernel trap, hang or touch memory outside the arrays it was given.
+ */
+#ifndef ASCAN_H_
+#define ASCAN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ASCAN_API __attribute__((visibility("default")))
+#else
+#define ASCAN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ASCAN_ABI_VERSION 1
+
+enum ascan_dtype { ASCAN_F32 = 0, ASCAN_F16 = 1, ASCAN_BF16 = 2 };
+enum ascan_index { ASCAN_I32 = 0, ASCAN_I64 = 1 };
+
+enum ascan_status {
+  ASCAN_OK = 0,
+  ASCAN_EINVAL = -1,         /* bad size, dtype, flag or null pointer */
+  ASCAN_EWORKSPACE = -2,     /* workspace missing, misaligned or too small */
+  ASCAN_ECUDA = -3,          /* a CUDA call failed (launch, memset) */
+  ASCAN_EDEVICE = -4,        /* no usable CUDA device */
+};
+
+/* Bits of the sticky per-device error word. */
+#define ASCAN_DEV_ERR_CU_END 0x1u       /* cu_seqlens[num_seq] != seq_total */
+#define ASCAN_DEV_ERR_CU_ORDER 0x2u     /* cu_seqlens not monotone / out of [0, seq_total] */
+#define ASCAN_DEV_ERR_LOOKBACK 0x4u     /* a tile predecessor never published (bounded wait expired) */
+
+/* Library identification. */
+ASCAN_API int ascan_abi_version(void);
+ASCAN_API const char* ascan_build_info(void);
+
+/* Human-readable text for an ascan_status value. */
+ASCAN_API const char* ascan_strerror(int status);
+
+/*
+ * Bytes of workspace that ascan_forward / ascan_backward need for
+ * num_channels * seq_total elements of dtype.
+ */
+ASCAN_API size_t ascan_workspace_size(int64_t num_channels, int64_t seq_total, int dtype);
+
+/*
+ * Forward scan.  Replaces the reference's two forward kernels and their
+ * dispatcher:
+ *   forward_scan_chunked            src/associative_scan_triton/_kernels.py:19-81
+ *   forward_scan_onepass_pipelined  src/associative_scan_triton/_kernels.py:84-168
+ *   forward_scan_full (routing)     src/associative_scan_triton/_dispatcher.py:12-70
+ * One kernel covers every sequence length; chunk_size / NUM_STAGES have no
+ * equivalent here.
+ *
+ *   gates, tokens      inputs [C, BL]
+ *   tokens_out         output [C, BL]; may equal tokens (in place, INPLACE=True)
+ *   gates_out          NULL, or output [C, BL] receiving the cumulative gate
+ *                      product from each sequence's first element (the
+ *                      reference's TESTING=True write-back); may equal gates
+ *   reverse            0: h[t] = g[t]h[t-1] + x[t];  1: h[t] = g[t]h[t+1] + x[t]
+ */
+ASCAN_API int ascan_forward(const void* gates, const void* tokens, void* tokens_out, void* gates_out,
+                  const void* cu_seqlens, int cu_index_type, int64_t num_seq,
+                  int64_t num_channels, int64_t seq_total, int dtype, int reverse,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Fused backward.  Replaces the reference's two backward kernels and their
+ * dispatcher:
+ *   backward_scan_fused               src/associative_scan_triton/_kernels.py:171-287
+ *   backward_scan_fused_single_chunk  src/associative_scan_triton/_kernels.py:290-374
+ *   backward_scan_fused_full          src/associative_scan_triton/_dispatcher.py:73-117
+ *
+ *   grad      dL/dh, [C, BL]
+ *   gates     the forward's gates
+ *   states    the forward's outputs h
+ *   d_tokens  output dL/dx = dh
+ *   d_gates   output dL/dg = dh[t] * h[t-1]   (causal; h[t+1] when causal == 0)
+ *   causal    1: adjoint of the causal scan (dh runs right to left);
+ *             0: adjoint of the reverse scan.
+ * Sequence boundaries: g past the end reads as 1, h before the start as 0.
+ */
+ASCAN_API int ascan_backward(const void* grad, const void* gates, const void* states, void* d_tokens,
+                   void* d_gates, const void* cu_seqlens, int cu_index_type, int64_t num_seq,
+                   int64_t num_channels, int64_t seq_total, int dtype, int causal,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Shift by one position inside every sequence and pad the vacated slot.
+ * Replaces _shift_pad_kernel / shift_pad_compiled
+ * (src/associative_scan_triton/_shift_pad.py:63-165) and the torch.roll
+ * variant shift_pad (_shift_pad.py:18-55).
+ *   backward 1: out[t] = data[t-1], pad at sequence starts cu[0..S-1]
+ *            0: out[t] = data[t+1], pad at sequence ends cu[1..S]-1
+ *   wrap     1: source index wraps around the row (torch.roll variant)
+ *            0: source index is clamped to [0, BL-1] (kernel variant)
+ * out must not overlap data.
+ */
+ASCAN_API int ascan_shift_pad(const void* data, void* out, const void* cu_seqlens, int cu_index_type,
+                    int64_t num_seq, int64_t num_channels, int64_t seq_total, int dtype,
+                    double pad_value, int backward, int wrap, void* stream);
+
+/*
+ * Read the sticky error word of `device` (ASCAN_DEV_ERR_* bits; 0 = none).
+ * Synchronises that device first.  *detail, if non-NULL, receives an
+ * implementation-defined integer about the first error (e.g. a tile index).
+ * Returns ASCAN_OK or a negative status.
+ */
+ASCAN_API int ascan_get_device_error(int device, unsigned int* code, long long* detail);
+
+/* Reset the sticky error word of `device`. */
+ASCAN_API int ascan_clear_device_error(int device);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASCAN_H_ */
