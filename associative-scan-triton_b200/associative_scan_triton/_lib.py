@@ -41,9 +41,13 @@ EXPORTED_SYMBOLS = (
   "ascan_forward",
   "ascan_backward",
   "ascan_shift_pad",
+  "ascan_set_implementation",
+  "ascan_get_implementation",
   "ascan_get_device_error",
   "ascan_clear_device_error",
 )
+
+IMPLEMENTATIONS = {"auto": 0, "simple": 1, "tma": 2}
 
 
 class ScanError(RuntimeError):
@@ -71,6 +75,10 @@ def _bind(lib) -> None:
   lib.ascan_backward.argtypes = [p, p, p, p, p, p, ci, i64, i64, i64, ci, ci, p, sz, p]
   lib.ascan_shift_pad.restype = ci
   lib.ascan_shift_pad.argtypes = [p, p, p, ci, i64, i64, i64, ci, ctypes.c_double, ci, ci, p]
+  lib.ascan_set_implementation.restype = ci
+  lib.ascan_set_implementation.argtypes = [ci]
+  lib.ascan_get_implementation.restype = ci
+  lib.ascan_get_implementation.argtypes = []
   lib.ascan_get_device_error.restype = ci
   lib.ascan_get_device_error.argtypes = [ci, ctypes.POINTER(ctypes.c_uint),
                                          ctypes.POINTER(ctypes.c_longlong)]
@@ -87,7 +95,7 @@ def load(path: str | os.PathLike | None = None):
   if not target.exists():
     _load_error = ScanError(
       f"native library {target} is missing; build it with "
-      "`python -m associative_scan_triton._build` (needs nvcc)")
+      "`python associative-scan-triton_b200/build_native.py` (needs nvcc)")
     raise _load_error
   lib = ctypes.CDLL(str(target))
   _bind(lib)
@@ -98,11 +106,14 @@ def load(path: str | os.PathLike | None = None):
 
 def try_load() -> bool:
   """Load the library if it exists; warn (do not raise) when it does not."""
+  global _lib
   try:
     load()
     return True
-  except ScanError as e:  # surfaced again, as an exception, by the first op
-    warnings.warn(str(e), RuntimeWarning, stacklevel=2)
+  except (ScanError, OSError, AttributeError) as e:  # raised again by the first op
+    _lib = None
+    warnings.warn(f"associative_scan_triton native library unusable: {e}", RuntimeWarning,
+                  stacklevel=2)
     return False
 
 
@@ -118,6 +129,20 @@ def set_sync_check(enabled: bool) -> None:
 
 def sync_check_enabled() -> bool:
   return _sync_check
+
+
+def set_implementation(name: str) -> None:
+  """Kernel family for the following calls: "auto" (the default choice),
+  "simple" (always the plain one-CTA-per-tile kernels) or "tma" (the
+  persistent TMA-pipelined kernels whenever pointers are 16-byte aligned)."""
+  rc = load().ascan_set_implementation(IMPLEMENTATIONS[name])
+  if rc != ASCAN_OK:
+    raise ScanError(f"ascan_set_implementation: {strerror(rc)}")
+
+
+def get_implementation() -> str:
+  code = load().ascan_get_implementation()
+  return {v: k for k, v in IMPLEMENTATIONS.items()}[int(code)]
 
 
 def strerror(status: int) -> str:

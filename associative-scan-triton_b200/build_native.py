@@ -1,10 +1,12 @@
 """Build the native library (CUDA for sm_100a) in place.
 
-    python -m associative_scan_triton._build [--force] [--verbose]
+    python associative-scan-triton_b200/build_native.py [--force] [--verbose]
 
 nvcc cross-compiles without a GPU, so this runs on a CPU-only host too.  The
-result, ``libascan_b200.so``, sits next to this file; it links the CUDA
-runtime statically so it loads on any host with an NVIDIA driver.
+result, ``associative_scan_triton/libascan_b200.so``, sits inside the package;
+it links the CUDA runtime statically so it loads on any host with an NVIDIA
+driver.  This module lives outside the package so that building never loads a
+(possibly stale) copy of the library into the process.
 """
 
 from __future__ import annotations
@@ -16,8 +18,8 @@ import subprocess
 import sys
 from pathlib import Path
 
-PKG_DIR = Path(__file__).resolve().parent
-DIST_DIR = PKG_DIR.parent
+DIST_DIR = Path(__file__).resolve().parent
+PKG_DIR = DIST_DIR / "associative_scan_triton"
 REPO_DIR = DIST_DIR.parent
 CSRC_DIR = DIST_DIR / "csrc"
 INCLUDE_DIR = REPO_DIR / "include"

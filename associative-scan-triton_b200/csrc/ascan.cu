@@ -23,7 +23,13 @@
 //     (a, b) = (gate of the neighbouring element, dy); the one-element shifts
 //     of the gates and of the states come from warp shuffles plus one scalar
 //     load at each warp edge, so no shifted copy is ever materialised.
+#include <cudaTypedefs.h>
 #include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <type_traits>
 
 #include "../../include/ascan.h"
 #include "ascan_device.cuh"
@@ -400,6 +406,416 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_kernel(const BwdArgs<T, Idx
   }
 }
 
+}  // namespace ascan
+
+#include "ascan_tma.cuh"
+
+namespace ascan {
+
+// ---------------------------------------------------------------------------
+// Persistent TMA kernels (see ascan_tma.cuh for the pipeline)
+// ---------------------------------------------------------------------------
+
+// Stages of the input ring: the deepest ring (at most 6) that fits next to the
+// output staging buffers in the 227 KB of shared memory a CTA may use.
+constexpr size_t kSmemBudget = 227 * 1024;
+
+template <typename T, int NIN, int NOUT, int NS = 6>
+constexpr int ring_depth() {
+  if constexpr (NS <= 2)
+    return 2;
+  else if constexpr (tma::smem_bytes<NIN, NOUT, NS, T>() <= kSmemBudget)
+    return NS;
+  else
+    return ring_depth<T, NIN, NOUT, NS - 1>();
+}
+
+// Producer warp of both kernels: tickets, TMA loads, per-tile metadata.
+// `Extra` fills the halo scalars and ragged-tail values of one stage.
+template <typename T, typename IdxT, bool REV, int NIN, int NOUT, int NS, typename Extra>
+__device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
+                                             const CUtensorMap* const* maps,
+                                             const tma::CuView<IdxT>& cu, int64_t N,
+                                             int64_t n_tma_total, uint32_t num_tiles,
+                                             uint32_t* ticket_ctr, const TileStatus& st, int lane,
+                                             Extra extra) {
+  using namespace tma;
+  if (lane == 0)
+    for (int k = 0; k < NIN; ++k) prefetch_map(maps[k]);
+  uint32_t stage = 0, phase = 0;
+  // pending[s]: the last use of stage s was a TMA load that the consumers have
+  // not been seen to release yet; last_parity[s]: the full-barrier phase of it.
+  bool pending[NS];
+  uint32_t last_parity[NS];
+#pragma unroll
+  for (int s = 0; s < NS; ++s) pending[s] = false, last_parity[s] = 0;
+  // The next ticket and the abort word are requested one tile ahead, so their
+  // global round trips overlap the current tile instead of serialising it.
+  uint32_t next_ticket = 0u, next_abort = 0u;
+  if (lane == 0) {
+    next_ticket = atomicAdd(ticket_ctr, 1u);
+    next_abort = ld_volatile_u32(st.abort);
+  }
+  while (true) {
+    uint32_t ticket = __shfl_sync(kFull, next_ticket, 0);
+    const uint32_t aborted = __shfl_sync(kFull, next_abort, 0);
+    if (ticket >= num_tiles || aborted) ticket = kDone;
+    if (lane == 0 && ticket != kDone) {
+      next_ticket = atomicAdd(ticket_ctr, 1u);
+      next_abort = ld_volatile_u32(st.abort);
+    }
+    if (!mbar_wait(&sm.empty[stage], phase ^ 1u)) {
+      if (lane == 0) {
+        report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffeull);
+        set_aborted(st);
+      }
+      break;
+    }
+    pending[stage] = false;  // its previous load was consumed and released
+    StageMeta<NIN, T>& m = sm.meta[stage];
+    if (ticket == kDone) {
+      if (lane == 0) {
+        m.ticket = kDone;
+        mbar_arrive(&sm.full[stage]);
+      }
+      break;
+    }
+    const uint32_t tile = REV ? num_tiles - 1u - ticket : ticket;
+    const int64_t p0 = static_cast<int64_t>(tile) * kTileElems;
+    const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow);
+    if (lane == 0) {
+      m.ticket = ticket;
+      mbar_expect_tx(&sm.full[stage], NIN * Fmt<T>::kBytes);
+      for (int k = 0; k < NIN; ++k) tma_load_2d(sm.in[stage][k], maps[k], 0, row, &sm.full[stage]);
+    }
+    pending[stage] = true;
+    last_parity[stage] = phase;
+    build_meta<IdxT, NIN, T>(m, cu, p0, N, n_tma_total, lane);
+    const int64_t rem = N - p0;
+    const uint32_t n_valid = static_cast<uint32_t>(rem < kTileElems ? rem : kTileElems);
+    int64_t nt = n_tma_total - p0;
+    nt = nt < 0 ? 0 : (nt > n_valid ? n_valid : nt);
+    extra(m, p0, static_cast<uint32_t>(nt), n_valid, lane);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.full[stage]);
+    if (++stage == NS) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+  // Never leave the CTA while a TMA load may still be writing shared memory:
+  // wait for every load whose stage was not released afterwards (its full
+  // barrier is still in the phase that load armed).
+#pragma unroll
+  for (int s = 0; s < NS; ++s)
+    if (pending[s]) mbar_wait(&sm.full[s], last_parity[s]);
+}
+
+template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS>
+__global__ void __launch_bounds__(tma::kThreads, 1)
+    scan_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_g,
+                        const __grid_constant__ CUtensorMap map_x,
+                        const __grid_constant__ CUtensorMap map_y,
+                        const __grid_constant__ CUtensorMap map_gout, const FwdArgs<T, IdxT> args,
+                        int64_t n_tma_total) {
+  using namespace tma;
+  constexpr int NIN = 2, NOUT = GATES_OUT ? 2 : 1;
+  using Sm = Smem<NIN, NOUT, NS, T>;
+  Sm& sm = smem_view<Sm>();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t S = args.S, BL = args.BL, N = args.N;
+
+  const bool cache_cu = (S + 1) <= kCuCache;
+  if (cache_cu)
+    for (int64_t i = tid; i <= S; i += tma::kThreads) sm.cu[i] = cu_at(args.cu, i, BL);
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kConsumerWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const CuView<IdxT> cu{args.cu, cache_cu ? sm.cu : nullptr, S, BL};
+
+  if (warp == kConsumerWarps) {
+    const CUtensorMap* maps[NIN] = {&map_g, &map_x};
+    run_producer<T, IdxT, REV, NIN, NOUT, NS>(
+        sm, maps, cu, N, n_tma_total, args.num_tiles, args.ticket, args.st, lane,
+        [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln) {
+          for (uint32_t e = n_tma + ln; e < n_valid; e += 32) {
+            m.tail[0][e - n_tma] = Cvt<T>::to(args.g[p0 + e]);
+            m.tail[1][e - n_tma] = Cvt<T>::to(args.x[p0 + e]);
+          }
+        });
+    return;
+  }
+
+  if (blockIdx.x == 0) validate_cu(args.cu, S, BL);
+  const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
+  uint32_t stage = 0, phase = 0, obuf = 0;
+  while (true) {
+    // Leave only together: a timed-out wait is agreed on by every consumer.
+    const bool got = mbar_wait(&sm.full[stage], phase);
+    if (consumers_any(!got)) {
+      if (tid == 0) {
+        report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull);
+        set_aborted(args.st);
+      }
+      break;
+    }
+    const StageMeta<NIN, T>& m = sm.meta[stage];
+    const uint32_t ticket = m.ticket;
+    if (ticket == kDone) break;
+    const int64_t p0 = m.p0;
+    const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
+    const bool has_outside = m.has_outside != 0u;
+    float a[kPerThread], b[kPerThread];
+    read_block<T, NIN>(sm.in[stage][0], m, 0, o, n_tma, n_valid, 1.f, a);
+    read_block<T, NIN>(sm.in[stage][1], m, 1, o, n_tma, n_valid, 0.f, b);
+    const uint32_t sh = o & 31u;
+    const uint32_t smask = (m.sbits[o >> 5] >> sh) & 0xffffu;
+    const uint32_t emask = (m.ebits[o >> 5] >> sh) & 0xffffu;
+    const uint32_t omask = has_outside ? (m.obits[o >> 5] >> sh) & 0xffffu : 0u;
+    const bool first_is_head =
+        REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[stage]);
+    if (++stage == NS) {
+      stage = 0;
+      phase ^= 1u;
+    }
+
+    const uint32_t head = REV ? emask : smask;
+    Pfx ex, wtot;
+    warp_scan<REV>(fold16<REV>(a, b, head), lane, ex, wtot);
+    if (tid == 0) bulk_wait_read<1>();  // staging buffer obuf is free again
+    const Pfx P = consumer_tile_prefix<REV>(sm, ex, wtot, first_is_head, ticket, args.st, warp,
+                                            lane);
+
+    float y[kPerThread], gp[kPerThread];
+    {
+      float h = P.b, ac = P.a;
+#pragma unroll
+      for (int jj = 0; jj < kPerThread; ++jj) {
+        const int j = REV ? kPerThread - 1 - jj : jj;
+        if ((head >> j) & 1u) {
+          h = b[j];
+          ac = a[j];
+        } else {
+          h = fmaf(a[j], h, b[j]);
+          ac *= a[j];
+        }
+        y[j] = h;
+        gp[j] = ac;
+      }
+    }
+    uint32_t valid = 0u;
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j)
+      if (o + j < n_valid) valid |= 1u << j;
+    valid &= ~omask;
+    uint32_t direct = valid;
+    if (!has_outside) {
+      write_block<T>(sm.out[obuf][0], o, y);
+      if constexpr (GATES_OUT) write_block<T>(sm.out[obuf][1], o, gp);
+      uint32_t below_tma = 0u;
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j)
+        if (o + j < n_tma) below_tma |= 1u << j;
+      direct &= ~below_tma;
+    }
+    if (direct) {
+      store_direct<T>(args.y, p0 + o, direct, y);
+      if constexpr (GATES_OUT) store_direct<T>(args.gout, p0 + o, direct, gp);
+    }
+    fence_async_smem();
+    consumer_sync();
+    if (tid == 0) {
+      if (!has_outside && n_tma > 0) {
+        const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow);
+        tma_store_2d(&map_y, 0, row, sm.out[obuf][0]);
+        if constexpr (GATES_OUT) tma_store_2d(&map_gout, 0, row, sm.out[obuf][1]);
+      }
+      bulk_commit();
+    }
+    obuf ^= 1u;
+  }
+  if (tid == 0) bulk_wait_all();
+}
+
+template <typename T, typename IdxT, bool CAUSAL, int NS>
+__global__ void __launch_bounds__(tma::kThreads, 1)
+    scan_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dy,
+                        const __grid_constant__ CUtensorMap map_g,
+                        const __grid_constant__ CUtensorMap map_h,
+                        const __grid_constant__ CUtensorMap map_dx,
+                        const __grid_constant__ CUtensorMap map_dg, const BwdArgs<T, IdxT> args,
+                        int64_t n_tma_total) {
+  using namespace tma;
+  constexpr bool REV = CAUSAL;
+  constexpr int NIN = 3, NOUT = 2;
+  using Sm = Smem<NIN, NOUT, NS, T>;
+  Sm& sm = smem_view<Sm>();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t S = args.S, BL = args.BL, N = args.N;
+
+  const bool cache_cu = (S + 1) <= kCuCache;
+  if (cache_cu)
+    for (int64_t i = tid; i <= S; i += tma::kThreads) sm.cu[i] = cu_at(args.cu, i, BL);
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kConsumerWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const CuView<IdxT> cu{args.cu, cache_cu ? sm.cu : nullptr, S, BL};
+
+  if (warp == kConsumerWarps) {
+    const CUtensorMap* maps[NIN] = {&map_dy, &map_g, &map_h};
+    run_producer<T, IdxT, REV, NIN, NOUT, NS>(
+        sm, maps, cu, N, n_tma_total, args.num_tiles, args.ticket, args.st, lane,
+        [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln) {
+          for (uint32_t e = n_tma + ln; e < n_valid; e += 32) {
+            m.tail[0][e - n_tma] = Cvt<T>::to(args.dy[p0 + e]);
+            m.tail[1][e - n_tma] = Cvt<T>::to(args.g[p0 + e]);
+            m.tail[2][e - n_tma] = Cvt<T>::to(args.h[p0 + e]);
+          }
+          if (ln == 0) {
+            const int64_t pn = p0 + kTileElems, pp = p0 - 1;
+            if (CAUSAL) {
+              m.halo[0] = pn < N ? Cvt<T>::to(args.g[pn]) : 1.f;
+              m.halo[1] = pp >= 0 ? Cvt<T>::to(args.h[pp]) : 0.f;
+            } else {
+              m.halo[0] = pp >= 0 ? Cvt<T>::to(args.g[pp]) : 1.f;
+              m.halo[1] = pn < N ? Cvt<T>::to(args.h[pn]) : 0.f;
+            }
+          }
+        });
+    return;
+  }
+
+  if (blockIdx.x == 0) validate_cu(args.cu, S, BL);
+  const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
+  uint32_t stage = 0, phase = 0, obuf = 0;
+  while (true) {
+    // Leave only together: a timed-out wait is agreed on by every consumer.
+    const bool got = mbar_wait(&sm.full[stage], phase);
+    if (consumers_any(!got)) {
+      if (tid == 0) {
+        report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull);
+        set_aborted(args.st);
+      }
+      break;
+    }
+    const StageMeta<NIN, T>& m = sm.meta[stage];
+    const uint32_t ticket = m.ticket;
+    if (ticket == kDone) break;
+    const int64_t p0 = m.p0;
+    const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
+    const bool has_outside = m.has_outside != 0u;
+    float dyv[kPerThread], gv[kPerThread], hv[kPerThread];
+    read_block<T, NIN>(sm.in[stage][0], m, 0, o, n_tma, n_valid, 0.f, dyv);
+    read_block<T, NIN>(sm.in[stage][1], m, 1, o, n_tma, n_valid, 1.f, gv);
+    read_block<T, NIN>(sm.in[stage][2], m, 2, o, n_tma, n_valid, 0.f, hv);
+    // neighbours across the thread boundary: from the tile, or the tile-edge halo
+    float g_nb, h_nb;
+    if (CAUSAL) {
+      g_nb = (o + kPerThread < static_cast<uint32_t>(kTileElems))
+                 ? tile_elem<T, NIN>(sm.in[stage][1], m, 1, o + kPerThread, n_tma, n_valid, 1.f)
+                 : m.halo[0];
+      h_nb = (o > 0) ? tile_elem<T, NIN>(sm.in[stage][2], m, 2, o - 1, n_tma, n_valid, 0.f)
+                     : m.halo[1];
+    } else {
+      g_nb = (o > 0) ? tile_elem<T, NIN>(sm.in[stage][1], m, 1, o - 1, n_tma, n_valid, 1.f)
+                     : m.halo[0];
+      h_nb = (o + kPerThread < static_cast<uint32_t>(kTileElems))
+                 ? tile_elem<T, NIN>(sm.in[stage][2], m, 2, o + kPerThread, n_tma, n_valid, 0.f)
+                 : m.halo[1];
+    }
+    const uint32_t sh = o & 31u;
+    const uint32_t smask = (m.sbits[o >> 5] >> sh) & 0xffffu;
+    const uint32_t emask = (m.ebits[o >> 5] >> sh) & 0xffffu;
+    const uint32_t omask = has_outside ? (m.obits[o >> 5] >> sh) & 0xffffu : 0u;
+    const bool first_is_head =
+        REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[stage]);
+    if (++stage == NS) {
+      stage = 0;
+      phase ^= 1u;
+    }
+
+    // a[t] = g[t+1], hn[t] = h[t-1] (causal) or the mirror image
+    if (CAUSAL) {
+#pragma unroll
+      for (int j = 0; j < kPerThread - 1; ++j) gv[j] = gv[j + 1];
+      gv[kPerThread - 1] = g_nb;
+#pragma unroll
+      for (int j = kPerThread - 1; j > 0; --j) hv[j] = hv[j - 1];
+      hv[0] = h_nb;
+    } else {
+#pragma unroll
+      for (int j = kPerThread - 1; j > 0; --j) gv[j] = gv[j - 1];
+      gv[0] = g_nb;
+#pragma unroll
+      for (int j = 0; j < kPerThread - 1; ++j) hv[j] = hv[j + 1];
+      hv[kPerThread - 1] = h_nb;
+    }
+    const uint32_t head = CAUSAL ? emask : smask;
+    const uint32_t tail = CAUSAL ? smask : emask;
+    Pfx ex, wtot;
+    warp_scan<REV>(fold16<REV>(gv, dyv, head), lane, ex, wtot);
+    if (tid == 0) bulk_wait_read<1>();
+    const Pfx P = consumer_tile_prefix<REV>(sm, ex, wtot, first_is_head, ticket, args.st, warp,
+                                            lane);
+    float dxo[kPerThread], dgo[kPerThread];
+    {
+      float d = P.b;
+#pragma unroll
+      for (int jj = 0; jj < kPerThread; ++jj) {
+        const int j = REV ? kPerThread - 1 - jj : jj;
+        d = ((head >> j) & 1u) ? dyv[j] : fmaf(gv[j], d, dyv[j]);
+        dxo[j] = d;
+        dgo[j] = ((tail >> j) & 1u) ? 0.f : d * hv[j];
+      }
+    }
+    uint32_t valid = 0u;
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j)
+      if (o + j < n_valid) valid |= 1u << j;
+    valid &= ~omask;
+    uint32_t direct = valid;
+    if (!has_outside) {
+      write_block<T>(sm.out[obuf][0], o, dxo);
+      write_block<T>(sm.out[obuf][1], o, dgo);
+      uint32_t below_tma = 0u;
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j)
+        if (o + j < n_tma) below_tma |= 1u << j;
+      direct &= ~below_tma;
+    }
+    if (direct) {
+      store_direct<T>(args.dx, p0 + o, direct, dxo);
+      store_direct<T>(args.dg, p0 + o, direct, dgo);
+    }
+    fence_async_smem();
+    consumer_sync();
+    if (tid == 0) {
+      if (!has_outside && n_tma > 0) {
+        const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow);
+        tma_store_2d(&map_dx, 0, row, sm.out[obuf][0]);
+        tma_store_2d(&map_dg, 0, row, sm.out[obuf][1]);
+      }
+      bulk_commit();
+    }
+    obuf ^= 1u;
+  }
+  if (tid == 0) bulk_wait_all();
+}
+
 // ---------------------------------------------------------------------------
 // shift_pad: out[t] = pad at boundaries, else data[t -/+ 1]
 // ---------------------------------------------------------------------------
@@ -467,6 +883,7 @@ static int carve(void* ws, size_t ws_bytes, int64_t n, Workspace& out) {
   char* base = static_cast<char*>(ws);
   const size_t tiles = tiles_of(n);
   out.ticket = reinterpret_cast<uint32_t*>(base);
+  out.st.abort = reinterpret_cast<uint32_t*>(base + 4);
   out.st.flags = reinterpret_cast<uint32_t*>(base + 256);
   out.st.vals = reinterpret_cast<float4*>(base + 256 + align256(tiles * sizeof(uint32_t)));
   out.clear_bytes = 256 + align256(tiles * sizeof(uint32_t));
@@ -482,6 +899,116 @@ static int launch_status() {
     return ASCAN_ECUDA;
   }
   return ASCAN_OK;
+}
+
+// ---- implementation choice ------------------------------------------------
+
+// 0: automatic (TMA kernels when the pointers and sizes allow), 1: always the
+// plain kernels, 2: TMA kernels whenever possible (same as 0 today).
+static int g_impl = -1;
+
+static int impl_mode() {
+  if (g_impl < 0) {
+    const char* e = getenv("ASCAN_IMPL");
+    g_impl = (e && strcmp(e, "simple") == 0) ? 1 : (e && strcmp(e, "tma") == 0) ? 2 : 0;
+  }
+  return g_impl;
+}
+
+// ---- TMA descriptors -------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// The flat array seen as `rows` rows of 128 bytes; one box = one 4096-element
+// tile, stored in shared memory with the 128-byte swizzle.
+template <typename T>
+static bool make_map(CUtensorMap* m, const void* base, int64_t rows) {
+  const auto fn = encode_fn();
+  if (!fn || rows <= 0 || rows > 0x7fffffffll) return false;
+  const CUtensorMapDataType dt =
+      std::is_same<T, float>::value    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+      : std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(tma::Fmt<T>::kElemsPerRow),
+                              static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {128};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(tma::Fmt<T>::kElemsPerRow),
+                             static_cast<cuuint32_t>(tma::Fmt<T>::kRows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return n;
+}
+
+// 1: launched, 0: not applicable (caller falls back to the plain kernel), <0: error
+template <typename T, typename IdxT, bool REV, bool GOUT>
+static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, cudaStream_t s) {
+  constexpr int NOUT = GOUT ? 2 : 1;
+  constexpr int NS = ring_depth<T, 2, NOUT>();
+  constexpr size_t smem = tma::smem_bytes<2, NOUT, NS, T>();
+  static_assert(smem <= kSmemBudget, "TMA forward ring does not fit in shared memory");
+  const int64_t rows = a.N / tma::Fmt<T>::kElemsPerRow;
+  CUtensorMap mg, mx, my, mgo;
+  if (!make_map<T>(&mg, a.g, rows) || !make_map<T>(&mx, a.x, rows) ||
+      !make_map<T>(&my, a.y, rows))
+    return 0;
+  if (GOUT) {
+    if (!make_map<T>(&mgo, a.gout, rows)) return 0;
+  } else {
+    mgo = my;
+  }
+  const int sms = sm_count();
+  if (sms <= 0) return 0;
+  auto kern = scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return ASCAN_ECUDA;
+  const unsigned grid = a.num_tiles < static_cast<uint32_t>(sms) ? a.num_tiles : sms;
+  kern<<<grid, tma::kThreads, smem, s>>>(mg, mx, my, mgo, a,
+                                          rows * tma::Fmt<T>::kElemsPerRow);
+  return launch_status() == ASCAN_OK ? 1 : ASCAN_ECUDA;
+}
+
+template <typename T, typename IdxT, bool CAUSAL>
+static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, cudaStream_t s) {
+  constexpr int NS = ring_depth<T, 3, 2>();
+  constexpr size_t smem = tma::smem_bytes<3, 2, NS, T>();
+  static_assert(smem <= kSmemBudget, "TMA backward ring does not fit in shared memory");
+  const int64_t rows = a.N / tma::Fmt<T>::kElemsPerRow;
+  CUtensorMap mdy, mg, mh, mdx, mdg;
+  if (!make_map<T>(&mdy, a.dy, rows) || !make_map<T>(&mg, a.g, rows) ||
+      !make_map<T>(&mh, a.h, rows) || !make_map<T>(&mdx, a.dx, rows) ||
+      !make_map<T>(&mdg, a.dg, rows))
+    return 0;
+  const int sms = sm_count();
+  if (sms <= 0) return 0;
+  auto kern = scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return ASCAN_ECUDA;
+  const unsigned grid = a.num_tiles < static_cast<uint32_t>(sms) ? a.num_tiles : sms;
+  kern<<<grid, tma::kThreads, smem, s>>>(mdy, mg, mh, mdx, mdg, a,
+                                          rows * tma::Fmt<T>::kElemsPerRow);
+  return launch_status() == ASCAN_OK ? 1 : ASCAN_ECUDA;
 }
 
 template <typename T, typename IdxT, int VEC>
@@ -518,6 +1045,14 @@ static int fwd_typed(const void* g, const void* x, void* y, void* gout, const vo
   a.st = w.st;
   const bool vec = aligned16(g) && aligned16(x) && aligned16(y) && (!gout || aligned16(gout));
   constexpr int kVec = 16 / sizeof(T);
+  if (vec && impl_mode() == 2 && a.N >= tma::Fmt<T>::kElemsPerRow) {
+    int rc;
+    if (reverse)
+      rc = gout ? launch_fwd_tma<T, IdxT, true, true>(a, s) : launch_fwd_tma<T, IdxT, true, false>(a, s);
+    else
+      rc = gout ? launch_fwd_tma<T, IdxT, false, true>(a, s) : launch_fwd_tma<T, IdxT, false, false>(a, s);
+    if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
+  }
   if (vec)
     fwd_dispatch<T, IdxT, kVec>(a, reverse != 0, gout != nullptr, s);
   else
@@ -553,6 +1088,10 @@ static int bwd_typed(const void* dy, const void* g, const void* h, void* dx, voi
   a.st = w.st;
   const bool vec = aligned16(dy) && aligned16(g) && aligned16(h) && aligned16(dx) && aligned16(dg);
   constexpr int kVec = 16 / sizeof(T);
+  if (vec && impl_mode() == 2 && a.N >= tma::Fmt<T>::kElemsPerRow) {
+    const int rc = causal ? launch_bwd_tma<T, IdxT, true>(a, s) : launch_bwd_tma<T, IdxT, false>(a, s);
+    if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
+  }
   if (vec)
     bwd_dispatch<T, IdxT, kVec>(a, causal != 0, s);
   else
@@ -687,6 +1226,14 @@ int ascan_shift_pad(const void* data, void* out, const void* cu_seqlens, int cu_
   ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_SP_CALL);
 #undef ASCAN_SP_CALL
 }
+
+int ascan_set_implementation(int impl) {
+  if (impl < 0 || impl > 2) return ASCAN_EINVAL;
+  g_impl = impl;
+  return ASCAN_OK;
+}
+
+int ascan_get_implementation(void) { return impl_mode(); }
 
 int ascan_get_device_error(int device, unsigned int* code, long long* detail) {
   int prev = -1;

@@ -23,7 +23,7 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr unsigned kFull = 0xffffffffu;
 // Every thread owns 16 elements per tile, so a tile is 4096 elements for
-// every dtype and load width (see TileGeom).
+// every dtype and load width.
 constexpr int kElemsPerThread = 16;
 constexpr int kTile = kThreads * kElemsPerThread;
 
@@ -386,10 +386,26 @@ __device__ __forceinline__ unsigned long long globaltimer() {
 }
 
 // Status slot of a ticket: flag word plus (aggregate a, b, inclusive a, b).
+// `abort` is a per-launch word: once any wait of the launch has given up, every
+// other wait returns at once, so a lost predecessor costs one timeout, not one
+// per tile.
 struct TileStatus {
   uint32_t* flags;
   float4* vals;
+  uint32_t* abort;
 };
+
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool launch_aborted(const TileStatus& st) {
+  return ld_volatile_u32(st.abort) != 0u;
+}
+
+__device__ __forceinline__ void set_aborted(const TileStatus& st) { atomicExch(st.abort, 1u); }
 
 __device__ __forceinline__ void publish(const TileStatus& st, uint32_t ticket, uint32_t kind,
                                         float a, float b) {
@@ -398,18 +414,23 @@ __device__ __forceinline__ void publish(const TileStatus& st, uint32_t ticket, u
   st_release(st.flags + ticket, kind);
 }
 
-// Wait (bounded) until the status of `ticket` is published; 0 on timeout.
+// Wait (bounded) until the status of `ticket` is published; 0 on timeout or
+// when the launch has been aborted.
 __device__ __forceinline__ uint32_t wait_status(const TileStatus& st, uint32_t ticket) {
   uint32_t s = ld_acquire(st.flags + ticket);
   if (s != kStatusNone) return s;
   const unsigned long long t0 = globaltimer();
-  unsigned ns = 32;
+  unsigned ns = 16;
   while (true) {
     __nanosleep(ns);
-    if (ns < 1024) ns <<= 1;
+    if (ns < 256) ns <<= 1;
     s = ld_acquire(st.flags + ticket);
     if (s != kStatusNone) return s;
-    if (globaltimer() - t0 > kLookbackTimeoutNs) return kStatusNone;
+    if (launch_aborted(st)) return kStatusNone;
+    if (globaltimer() - t0 > kLookbackTimeoutNs) {
+      set_aborted(st);
+      return kStatusNone;
+    }
   }
 }
 

@@ -133,6 +133,21 @@ ASCAN_API int ascan_shift_pad(const void* data, void* out, const void* cu_seqlen
                     double pad_value, int backward, int wrap, void* stream);
 
 /*
+ * Kernel family used by the calls that follow (process-wide):
+ *   0  automatic (the default; env ASCAN_IMPL=simple|tma overrides it):
+ *      currently the plain kernels, the faster family on B200 so far
+ *   1  always the plain kernels (128-bit loads, one CTA per tile)
+ *   2  the persistent TMA-pipelined kernels whenever every pointer is
+ *      16-byte aligned and the array holds at least one 128-byte row,
+ *      the plain kernels otherwise
+ * Both families compute the same results; the switch exists for testing
+ * and measurement.  No counterpart in the reference, which has one
+ * Triton kernel per case.
+ */
+ASCAN_API int ascan_set_implementation(int impl);
+ASCAN_API int ascan_get_implementation(void);
+
+/*
  * Read the sticky error word of `device` (ASCAN_DEV_ERR_* bits; 0 = none).
  * Synchronises that device first.  *detail, if non-NULL, receives an
  * implementation-defined integer about the first error (e.g. a tile index).

@@ -31,14 +31,14 @@ def _build_native() -> None:
   from oracle import oracle as _oracle
 
   _oracle.build()
-  from associative_scan_triton import _build
+  import build_native
 
-  if not _build.up_to_date():
+  if not build_native.up_to_date():
     try:
-      _build._nvcc()
+      build_native._nvcc()
     except RuntimeError:
       return
-    _build.build()
+    build_native.build()
 
 
 _build_native()
@@ -70,6 +70,16 @@ def _cuda_hygiene():
   if torch.cuda.is_available():
     torch.cuda.synchronize()
   gc.collect()
+
+
+@pytest.fixture(params=["tma", "simple"])
+def impl(request):
+  """Run a test under both kernel families (persistent TMA and plain)."""
+  from associative_scan_triton import _lib
+
+  _lib.set_implementation(request.param)
+  yield request.param
+  _lib.set_implementation("auto")
 
 
 def first_order_op(fl, xl, fr, xr):

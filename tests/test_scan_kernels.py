@@ -180,7 +180,7 @@ def test_onepass_and_backward_launchers():
 # --- the reference's own outputs (tests/golden, made by running the reference) ---------
 
 @pytest.mark.parametrize("case", golden_case_names("fwd"))
-def test_forward_matches_reference_golden(case):
+def test_forward_matches_reference_golden(case, impl):
   z, meta = golden_cases()
   m = meta[case]
   dtype = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}[m["dtype"]]
@@ -209,7 +209,7 @@ def test_forward_matches_reference_golden(case):
 
 
 @pytest.mark.parametrize("case", golden_case_names("bwd"))
-def test_backward_matches_reference_golden(case):
+def test_backward_matches_reference_golden(case, impl):
   z, meta = golden_cases()
   m = meta[case]
   dtype = {"float32": torch.float32, "float16": torch.float16}[m["dtype"]]
@@ -243,13 +243,16 @@ EDGE_CASES = [
   (2, [512] * 24),
   (1, [0, 5, 0, 0, 9, 0]),        # empty sequences
   (300, [3, 2]),                  # rows of 5 elements, tile spans 800+ rows
+  (3, [4096 * 5 + 31]),           # ragged tail shorter than one 128-byte row
+  (1, [12345, 54321]),
+  (2, [1] * 700 + [9000]),        # hundreds of heads in one tile
 ]
 
 
 @pytest.mark.parametrize(("C", "seqlens"), EDGE_CASES)
 @pytest.mark.parametrize("reverse", [False, True])
 @pytest.mark.parametrize("cu_dtype", [torch.int32, torch.int64])
-def test_forward_edge_cases(C, seqlens, reverse, cu_dtype):
+def test_forward_edge_cases(C, seqlens, reverse, cu_dtype, impl):
   BL = sum(seqlens)
   g, x = make_inputs(C, BL, gate="long", seed=C * 7 + BL)
   cu = cu_of(seqlens, dtype=cu_dtype)
@@ -268,7 +271,7 @@ def test_forward_edge_cases(C, seqlens, reverse, cu_dtype):
 
 @pytest.mark.parametrize(("C", "seqlens"), EDGE_CASES)
 @pytest.mark.parametrize("causal", [True, False])
-def test_backward_edge_cases(C, seqlens, causal):
+def test_backward_edge_cases(C, seqlens, causal, impl):
   BL = sum(seqlens)
   g, x = make_inputs(C, BL, gate="long", seed=C * 11 + BL)
   dy = torch.randn_like(x)
@@ -306,7 +309,7 @@ def test_misaligned_views(offset, dtype):
   assert_close_to_gold(dg, gdg, dtype, "misaligned dg")
 
 
-def test_positions_outside_sequences_are_untouched():
+def test_positions_outside_sequences_are_untouched(impl):
   # cu[0] > 0: the head of every row belongs to no sequence (reference: masked)
   C, BL = 4, 5000
   g, x = make_inputs(C, BL)
@@ -321,7 +324,7 @@ def test_positions_outside_sequences_are_untouched():
 
 
 @pytest.mark.parametrize("reverse", [False, True])
-def test_boundaries_are_bit_exact_and_isolated(reverse):
+def test_boundaries_are_bit_exact_and_isolated(reverse, impl):
   # the first element of a sequence (in scan order) is its token, bit for bit,
   # and nothing -- not even Inf/NaN -- leaks across a boundary
   C, seqlens = 5, [1000, 3000, 4096, 123, 9000]
@@ -347,7 +350,7 @@ def test_boundaries_are_bit_exact_and_isolated(reverse):
 
 
 @pytest.mark.parametrize("causal", [True, False])
-def test_backward_boundaries_exact(causal):
+def test_backward_boundaries_exact(causal, impl):
   C, seqlens = 3, [700, 5000, 1]
   BL = sum(seqlens)
   g, x = make_inputs(C, BL)
@@ -410,3 +413,42 @@ def test_nonzero_stream_and_second_device_index():
   s.synchronize()
   gold_y, _ = oracle.scan_fwd(g, x, cu)
   assert_close_to_gold(y, gold_y, torch.float32, "y on side stream")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_both_kernel_families_agree(dtype, reverse):
+  # the persistent TMA kernels and the plain kernels compute the same scan
+  # (different association order, so compare both to the oracle and to each other)
+  from associative_scan_triton import _lib
+  seqlens = [5000, 77, 4096, 1, 20000, 333]
+  C = 9
+  BL = sum(seqlens)
+  g, x = make_inputs(C, BL, dtype=dtype, gate="long")
+  cu = cu_of(seqlens)
+  outs = {}
+  try:
+    for name in ("tma", "simple"):
+      _lib.set_implementation(name)
+      y = torch.empty_like(x)
+      gp = g.clone()
+      ast.forward_scan_full(gp, x, cu, (len(seqlens), 1, C), REVERSE=reverse, CHUNK_SIZE=2,
+                            TESTING=True, tokens_out=y)
+      dy = torch.ones_like(x)
+      dx, dg = torch.empty_like(x), torch.empty_like(x)
+      ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, (len(seqlens), 1, C), CHUNK_SIZE=2,
+                                   CAUSAL=not reverse)
+      outs[name] = (y, gp, dx, dg)
+  finally:
+    _lib.set_implementation("auto")
+  gold_y, gold_a = oracle.scan_fwd(g, x, cu, reverse=reverse)
+  for name, (y, gp, dx, dg) in outs.items():
+    assert_close_to_gold(y, gold_y, dtype, f"{name} y")
+    assert_close_to_gold(gp, gold_a, dtype, f"{name} gate products")
+    gdx, gdg = oracle.scan_bwd(torch.ones_like(x), g, outs["tma"][0], cu, causal=not reverse)
+    assert_close_to_gold(dx, gdx, dtype, f"{name} dx")
+  # the two families against each other, with the oracle tests' scale-aware bound
+  for i in range(4):
+    ref = outs["simple"][i].double().cpu().numpy()
+    assert_close_to_gold(outs["tma"][i], ref, dtype, f"tma vs simple output {i}",
+                         rtol=2 * rtol_of(dtype))
