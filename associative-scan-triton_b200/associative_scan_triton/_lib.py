@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
   "ascan_strerror",
   "ascan_workspace_size",
   "ascan_forward",
+  "ascan_forward_noalloc",
   "ascan_backward",
   "ascan_shift_pad",
   "ascan_set_implementation",

@@ -40,6 +40,12 @@ namespace ascan {
 __device__ unsigned int g_err_code = 0;
 __device__ unsigned long long g_err_detail = 0;
 
+// Fixed scratch of ascan_forward_noalloc: the look-back workspace for callers
+// that cannot allocate device memory.  Every device that loads this library
+// holds these bytes until the process exits; all calls share them.
+constexpr size_t kNoAllocScratchBytes = ASCAN_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
 __device__ __forceinline__ void report(unsigned int bits, unsigned long long detail) {
   if (atomicOr(&g_err_code, bits) == 0u) atomicExch(&g_err_detail, detail);
 }
@@ -1141,6 +1147,9 @@ const char* ascan_strerror(int status) {
     case ASCAN_EWORKSPACE: return "workspace missing, not 256-byte aligned or too small";
     case ASCAN_ECUDA: return "CUDA launch or memset failed";
     case ASCAN_EDEVICE: return "no usable CUDA device";
+    case ASCAN_ETOOLARGE:
+      return "problem too large for the fixed scratch of ascan_forward_noalloc "
+             "(num_channels * seq_total must be <= ASCAN_NOALLOC_MAX_ELEMENTS)";
     default: return "unknown ascan status";
   }
 }
@@ -1225,6 +1234,56 @@ int ascan_shift_pad(const void* data, void* out, const void* cu_seqlens, int cu_
                         backward, wrap, s)
   ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_SP_CALL);
 #undef ASCAN_SP_CALL
+}
+
+// Device address of g_noalloc_scratch on `device` (the current device).  In
+// host code the symbol is only a host-side stand-in, so the address is taken
+// once per device with cudaGetSymbolAddress and cached.
+static void* noalloc_scratch(int device, int* status) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void* ptrs[kMaxDevices] = {};
+  if (device < 0 || device >= kMaxDevices) {
+    *status = ASCAN_EDEVICE;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[device] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      *status = ASCAN_ECUDA;
+      return nullptr;
+    }
+    ptrs[device] = p;
+  }
+  return ptrs[device];
+}
+
+int ascan_forward_noalloc(const void* gates, const void* tokens, void* tokens_out,
+                          void* gates_out, const void* cu_seqlens, int cu_index_type,
+                          int64_t num_seq, int64_t num_channels, int64_t seq_total, int dtype,
+                          int reverse, void* stream) {
+  int rc = check_common(cu_seqlens, cu_index_type, num_seq, num_channels, seq_total, dtype);
+  if (rc != ASCAN_OK) return rc;
+  if (!gates || !tokens || !tokens_out) return ASCAN_EINVAL;
+  const int64_t n = num_channels * seq_total;
+  if (n == 0 || num_seq == 0) return ASCAN_OK;
+  if (workspace_bytes_for(n) > kNoAllocScratchBytes) return ASCAN_ETOOLARGE;
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) return ASCAN_EDEVICE;
+  void* ws = noalloc_scratch(device, &rc);
+  if (ws == nullptr) return rc;
+  Workspace w;
+  rc = carve(ws, kNoAllocScratchBytes, n, w);
+  if (rc != ASCAN_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the previous call's tickets and tile flags are still in the array
+  if (cudaMemsetAsync(w.ticket, 0, w.clear_bytes, s) != cudaSuccess) return ASCAN_ECUDA;
+#define ASCAN_FWD_NA_CALL(T, I)                                                                \
+  fwd_typed<T, I>(gates, tokens, tokens_out, gates_out, cu_seqlens, num_seq, num_channels,     \
+                  seq_total, reverse, w, s)
+  ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_FWD_NA_CALL);
+#undef ASCAN_FWD_NA_CALL
 }
 
 int ascan_set_implementation(int impl) {

@@ -55,6 +55,7 @@ enum ascan_status {
   ASCAN_EWORKSPACE = -2,     /* workspace missing, misaligned or too small */
   ASCAN_ECUDA = -3,          /* a CUDA call failed (launch, memset) */
   ASCAN_EDEVICE = -4,        /* no usable CUDA device */
+  ASCAN_ETOOLARGE = -5,      /* problem exceeds the fixed scratch of ascan_forward_noalloc */
 };
 
 /* Bits of the sticky per-device error word. */
@@ -116,6 +117,40 @@ ASCAN_API int ascan_backward(const void* grad, const void* gates, const void* st
                    void* d_gates, const void* cu_seqlens, int cu_index_type, int64_t num_seq,
                    int64_t num_channels, int64_t seq_total, int dtype, int causal,
                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Forward scan that allocates nothing: ascan_forward without the workspace
+ * arguments.  No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory when they call the scan --
+ * for example a serving loop that runs under a fixed memory budget and owns
+ * no allocator, a plugin whose host application hands it only the input and
+ * output buffers, or a foreign-language binding of this C ABI that has no
+ * access to torch's caching allocator.  They still pass their inputs and
+ * outputs; the look-back scratch (tile tickets and status records) lives in
+ * a fixed array of ASCAN_NOALLOC_SCRATCH_BYTES inside this library, which
+ * every GPU that loads the library holds until the process exits.
+ *
+ * Limits and rules:
+ *   - num_channels * seq_total <= ASCAN_NOALLOC_MAX_ELEMENTS, otherwise
+ *     ASCAN_ETOOLARGE is returned and nothing is launched;
+ *   - every call on a device uses the same array: calls that overlap on the
+ *     GPU (two streams, two threads) race and corrupt each other's results --
+ *     serialise them, or use ascan_forward with separate workspaces;
+ *   - the array keeps the previous call's contents; each call clears the part
+ *     that must start at zero before its kernel runs (stream-ordered);
+ *   - the first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current) and caches it; make
+ *     that first call before any stream capture begins;
+ *   - no cudaMalloc, cudaFree or other allocating routine is called.
+ * Arguments, results and other return codes are those of ascan_forward.
+ */
+#define ASCAN_NOALLOC_SCRATCH_BYTES (2u << 20)
+#define ASCAN_NOALLOC_MAX_ELEMENTS 429391872ll /* 104832 tiles of 4096 elements */
+ASCAN_API int ascan_forward_noalloc(const void* gates, const void* tokens, void* tokens_out,
+                                    void* gates_out, const void* cu_seqlens, int cu_index_type,
+                                    int64_t num_seq, int64_t num_channels, int64_t seq_total,
+                                    int dtype, int reverse, void* stream);
 
 /*
  * Shift by one position inside every sequence and pad the vacated slot.
