@@ -48,7 +48,7 @@ EXPORTED_SYMBOLS = (
   "ascan_clear_device_error",
 )
 
-IMPLEMENTATIONS = {"auto": 0, "simple": 1, "tma": 2}
+IMPLEMENTATIONS = {"auto": 0, "simple": 1, "tma": 2, "tma-flat": 3, "tma-row": 4}
 
 
 class ScanError(RuntimeError):
@@ -134,8 +134,9 @@ def sync_check_enabled() -> bool:
 
 def set_implementation(name: str) -> None:
   """Kernel family for the following calls: "auto" (the default choice),
-  "simple" (always the plain one-CTA-per-tile kernels) or "tma" (the
-  persistent TMA-pipelined kernels whenever pointers are 16-byte aligned)."""
+  "simple" (always the plain one-CTA-per-tile kernels), "tma" (the
+  persistent TMA-pipelined kernels whenever pointers are 16-byte aligned),
+  "tma-flat" / "tma-row" (the TMA kernels with the tile order forced)."""
   rc = load().ascan_set_implementation(IMPLEMENTATIONS[name])
   if rc != ASCAN_OK:
     raise ScanError(f"ascan_set_implementation: {strerror(rc)}")

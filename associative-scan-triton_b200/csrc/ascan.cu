@@ -95,40 +95,9 @@ __device__ __forceinline__ Pfx tile_prefix(Pfx warp_total, bool first_is_head, u
       publish(st, ticket, inclusive ? kStatusInclusive : kStatusAggregate, tot.a, tot.b);
     }
     if (need_lookback) {
-      int64_t base = static_cast<int64_t>(ticket) - 1;
       bool timed_out = false;
-      while (true) {
-        const int64_t q = base - lane;
-        Pfx x = pfx_empty();
-        bool inc = true;
-        if (q >= 0) {
-          const uint32_t s = wait_status(st, static_cast<uint32_t>(q));
-          if (s == kStatusInclusive || s == kStatusAggregate) {
-            const float2 v = ld_relaxed_f2(reinterpret_cast<const float*>(st.vals + q) +
-                                           (s == kStatusInclusive ? 2 : 0));
-            x = Pfx{v.x, v.y, kValid};
-            inc = (s == kStatusInclusive);
-          } else {
-            timed_out = true;  // treated as an empty inclusive prefix
-          }
-        }
-        const unsigned incmask = __ballot_sync(kFull, inc);
-        const int stop = incmask ? (__ffs(incmask) - 1) : 31;
-        if (lane > stop) x = pfx_empty();
-        // x_stop o ... o x_1 o x_0 (a higher lane is an earlier tile)
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          Pfx o{__shfl_down_sync(kFull, x.a, off), __shfl_down_sync(kFull, x.b, off),
-                __shfl_down_sync(kFull, x.f, off)};
-          if (lane + off < 32) x = compose(o, x);
-        }
-        const Pfx part{__shfl_sync(kFull, x.a, 0), __shfl_sync(kFull, x.b, 0),
-                       __shfl_sync(kFull, x.f, 0)};
-        te = compose(part, te);
-        if (incmask) break;
-        base -= 32;
-      }
-      if (__any_sync(kFull, timed_out) && lane == 0) report(ASCAN_DEV_ERR_LOOKBACK, ticket);
+      te = lookback_warp<kLookbackPerLane>(st, ticket, lane, &timed_out);
+      if (timed_out && lane == 0) report(ASCAN_DEV_ERR_LOOKBACK, ticket);
       if (lane == 0) {
         if (!(tot.f & kHead)) {
           const Pfx inc = compose(te, tot);
@@ -436,15 +405,22 @@ constexpr int ring_depth() {
     return ring_depth<T, NIN, NOUT, NS - 1>();
 }
 
-// Producer warp of both kernels: tickets, TMA loads, per-tile metadata.
-// `Extra` fills the halo scalars and ragged-tail values of one stage.
+// Producer warp of both kernels: TMA loads and per-tile metadata.  Tickets
+// are dealt round-robin in scan order (CTA b takes tickets b, b+G, b+2G, ...,
+// G = gridDim.x) and the launch is cooperative, so every CTA is resident and
+// the CTAs move through the tickets in waves: a tile's predecessor is in the
+// same or an earlier wave.  In row mode the producer also copies the status
+// slot of the tile's predecessor (many waves older when rows >> CTAs) into the
+// stage metadata with an asynchronous bulk copy, so the consumers usually find
+// the carry-in there instead of polling global memory, and the producer never
+// waits for that read.
+// `Extra` fills the halo scalars and the ragged tail of one stage.
 template <typename T, typename IdxT, bool REV, int NIN, int NOUT, int NS, typename Extra>
 __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
                                              const CUtensorMap* const* maps,
                                              const tma::CuView<IdxT>& cu, int64_t N,
-                                             int64_t n_tma_total, uint32_t num_tiles,
-                                             uint32_t* ticket_ctr, const TileStatus& st, int lane,
-                                             Extra extra) {
+                                             int64_t n_tma_total, const tma::TileSched& sch,
+                                             const TileStatus& st, int lane, Extra extra) {
   using namespace tma;
   if (lane == 0)
     for (int k = 0; k < NIN; ++k) prefetch_map(maps[k]);
@@ -455,21 +431,22 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
   uint32_t last_parity[NS];
 #pragma unroll
   for (int s = 0; s < NS; ++s) pending[s] = false, last_parity[s] = 0;
-  // The next ticket and the abort word are requested one tile ahead, so their
-  // global round trips overlap the current tile instead of serialising it.
-  uint32_t next_ticket = 0u, next_abort = 0u;
-  if (lane == 0) {
-    next_ticket = atomicAdd(ticket_ctr, 1u);
-    next_abort = ld_volatile_u32(st.abort);
+  const int64_t BL = cu.BL;
+  const uint32_t G = gridDim.x;
+  const uint32_t num_tiles = sch.num_tiles;
+  // flat mode: row position of the current tile's first element, advanced by
+  // the (constant) distance between this CTA's consecutive tiles
+  const int64_t step = (static_cast<int64_t>(G) * kTileElems) % BL;
+  uint32_t ticket = blockIdx.x;
+  int64_t t_flat = 0;
+  if (!sch.row_mode && ticket < num_tiles) {
+    const uint32_t tile0 = REV ? num_tiles - 1u - ticket : ticket;
+    t_flat = (static_cast<int64_t>(tile0) * kTileElems) % BL;
   }
+  uint32_t abort_seen = 0u;
   while (true) {
-    uint32_t ticket = __shfl_sync(kFull, next_ticket, 0);
-    const uint32_t aborted = __shfl_sync(kFull, next_abort, 0);
-    if (ticket >= num_tiles || aborted) ticket = kDone;
-    if (lane == 0 && ticket != kDone) {
-      next_ticket = atomicAdd(ticket_ctr, 1u);
-      next_abort = ld_volatile_u32(st.abort);
-    }
+    if (ticket >= num_tiles || abort_seen) ticket = kDone;
+    const uint32_t abort_next = (lane == 0 && ticket != kDone) ? ld_volatile_u32(st.abort) : 0u;
     if (!mbar_wait(&sm.empty[stage], phase ^ 1u)) {
       if (lane == 0) {
         report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffeull);
@@ -486,28 +463,52 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
       }
       break;
     }
-    const uint32_t tile = REV ? num_tiles - 1u - ticket : ticket;
-    const int64_t p0 = static_cast<int64_t>(tile) * kTileElems;
+    int64_t p0, t0, limit;
+    if (sch.row_mode) {
+      const uint32_t j = ticket / sch.rows;
+      const uint32_t c = ticket - j * sch.rows;
+      const uint32_t jj = REV ? sch.tiles_per_row - 1u - j : j;
+      t0 = static_cast<int64_t>(jj) * kTileElems;
+      p0 = static_cast<int64_t>(c) * BL + t0;
+      limit = static_cast<int64_t>(c) * BL + BL;
+    } else {
+      const uint32_t tile = REV ? num_tiles - 1u - ticket : ticket;
+      p0 = static_cast<int64_t>(tile) * kTileElems;
+      t0 = t_flat;
+      limit = N;
+    }
     const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow);
+    const bool read_pred = sch.row_mode && ticket >= sch.stride;
     if (lane == 0) {
       m.ticket = ticket;
-      mbar_expect_tx(&sm.full[stage], NIN * Fmt<T>::kBytes);
+      if (!read_pred) m.te_raw[1] = m.te_raw[3] = kStatusNone;
+      mbar_expect_tx(&sm.full[stage], NIN * Fmt<T>::kBytes + (read_pred ? 16u : 0u));
       for (int k = 0; k < NIN; ++k) tma_load_2d(sm.in[stage][k], maps[k], 0, row, &sm.full[stage]);
+      if (read_pred) bulk_load(m.te_raw, st.slots + (ticket - sch.stride), 16u, &sm.full[stage]);
     }
     pending[stage] = true;
     last_parity[stage] = phase;
-    build_meta<IdxT, NIN, T>(m, cu, p0, N, n_tma_total, lane);
-    const int64_t rem = N - p0;
+    build_meta<IdxT, NIN, T>(m, cu, p0, t0, limit, n_tma_total, lane);
+    const int64_t rem = limit - p0;
     const uint32_t n_valid = static_cast<uint32_t>(rem < kTileElems ? rem : kTileElems);
     int64_t nt = n_tma_total - p0;
     nt = nt < 0 ? 0 : (nt > n_valid ? n_valid : nt);
-    extra(m, p0, static_cast<uint32_t>(nt), n_valid, lane);
+    extra(m, p0, static_cast<uint32_t>(nt), n_valid, lane, &sm.full[stage]);
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.full[stage]);
     if (++stage == NS) {
       stage = 0;
       phase ^= 1u;
     }
+    ticket += G;
+    if (REV) {
+      t_flat -= step;
+      if (t_flat < 0) t_flat += BL;
+    } else {
+      t_flat += step;
+      if (t_flat >= BL) t_flat -= BL;
+    }
+    abort_seen = __shfl_sync(kFull, abort_next, 0);
   }
   // Never leave the CTA while a TMA load may still be writing shared memory:
   // wait for every load whose stage was not released afterwards (its full
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
                         const __grid_constant__ CUtensorMap map_x,
                         const __grid_constant__ CUtensorMap map_y,
                         const __grid_constant__ CUtensorMap map_gout, const FwdArgs<T, IdxT> args,
-                        int64_t n_tma_total) {
+                        int64_t n_tma_total, const tma::TileSched sch) {
   using namespace tma;
   constexpr int NIN = 2, NOUT = GATES_OUT ? 2 : 1;
   using Sm = Smem<NIN, NOUT, NS, T>;
@@ -534,11 +535,16 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
   const bool cache_cu = (S + 1) <= kCuCache;
   if (cache_cu)
     for (int64_t i = tid; i <= S; i += tma::kThreads) sm.cu[i] = cu_at(args.cu, i, BL);
+  if (tid < kXsRing * (kConsumerWarps + 1)) {
+    float4* f = &sm.xs[0].warp[0] + tid;
+    f->w = __uint_as_float(kNoTag);
+  }
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kConsumerWarps);
     }
+    sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -547,8 +553,9 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
   if (warp == kConsumerWarps) {
     const CUtensorMap* maps[NIN] = {&map_g, &map_x};
     run_producer<T, IdxT, REV, NIN, NOUT, NS>(
-        sm, maps, cu, N, n_tma_total, args.num_tiles, args.ticket, args.st, lane,
-        [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln) {
+        sm, maps, cu, N, n_tma_total, sch, args.st, lane,
+        [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
+            uint64_t*) {
           for (uint32_t e = n_tma + ln; e < n_valid; e += 32) {
             m.tail[0][e - n_tma] = Cvt<T>::to(args.g[p0 + e]);
             m.tail[1][e - n_tma] = Cvt<T>::to(args.x[p0 + e]);
@@ -559,15 +566,16 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
 
   if (blockIdx.x == 0) validate_cu(args.cu, S, BL);
   const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
-  uint32_t stage = 0, phase = 0, obuf = 0;
-  while (true) {
-    // Leave only together: a timed-out wait is agreed on by every consumer.
-    const bool got = mbar_wait(&sm.full[stage], phase);
-    if (consumers_any(!got)) {
-      if (tid == 0) {
-        report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull);
-        set_aborted(args.st);
-      }
+  const ThreadChunks<T> tc(o);
+  const uint32_t bit_word = o >> 5, bit_shift = o & 31u;
+  constexpr int kPartRows = Fmt<T>::kRows / kConsumerWarps;    // this warp's slice of a tile
+  constexpr int kPartBytes = Fmt<T>::kBytes / kConsumerWarps;
+  uint32_t stage = 0, phase = 0, obuf = 0, xi = 0;
+  bool ok = true;
+  while (ok) {
+    const bool got = __all_sync(kFull, mbar_wait(&sm.full[stage], phase));
+    if (!got || *reinterpret_cast<volatile int*>(&sm.abort)) {
+      ok = false;
       break;
     }
     const StageMeta<NIN, T>& m = sm.meta[stage];
@@ -577,14 +585,15 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
     const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
     const bool has_outside = m.has_outside != 0u;
     float a[kPerThread], b[kPerThread];
-    read_block<T, NIN>(sm.in[stage][0], m, 0, o, n_tma, n_valid, 1.f, a);
-    read_block<T, NIN>(sm.in[stage][1], m, 1, o, n_tma, n_valid, 0.f, b);
-    const uint32_t sh = o & 31u;
-    const uint32_t smask = (m.sbits[o >> 5] >> sh) & 0xffffu;
-    const uint32_t emask = (m.ebits[o >> 5] >> sh) & 0xffffu;
-    const uint32_t omask = has_outside ? (m.obits[o >> 5] >> sh) & 0xffffu : 0u;
+    read_block<T, NIN>(sm.in[stage][0], tc, m, 0, o, n_tma, n_valid, 1.f, a);
+    read_block<T, NIN>(sm.in[stage][1], tc, m, 1, o, n_tma, n_valid, 0.f, b);
+    const uint32_t head =
+        ((REV ? m.ebits[bit_word] : m.sbits[bit_word]) >> bit_shift) & 0xffffu;
+    const uint32_t omask = has_outside ? (m.obits[bit_word] >> bit_shift) & 0xffffu : 0u;
     const bool first_is_head =
         REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
+    const bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
+    const Pfx te_meta{__uint_as_float(m.te_raw[0]), __uint_as_float(m.te_raw[2]), kValid};
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[stage]);
     if (++stage == NS) {
@@ -592,62 +601,62 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
       phase ^= 1u;
     }
 
-    const uint32_t head = REV ? emask : smask;
     Pfx ex, wtot;
-    warp_scan<REV>(fold16<REV>(a, b, head), lane, ex, wtot);
-    if (tid == 0) bulk_wait_read<1>();  // staging buffer obuf is free again
-    const Pfx P = consumer_tile_prefix<REV>(sm, ex, wtot, first_is_head, ticket, args.st, warp,
-                                            lane);
-
-    float y[kPerThread], gp[kPerThread];
-    {
-      float h = P.b, ac = P.a;
+    warp_scan<REV>(fold16_inplace<REV>(a, b, head), lane, ex, wtot);
+    const Pfx P = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
+                                        sch.stride, te_known, te_meta, warp, lane, ok);
+    // a, b hold the local prefixes: h = A_loc * carry + B_loc before the first head
+    const uint32_t cm = carry_mask<REV>(head);
+    if (cm == 0xffffu) {
 #pragma unroll
-      for (int jj = 0; jj < kPerThread; ++jj) {
-        const int j = REV ? kPerThread - 1 - jj : jj;
-        if ((head >> j) & 1u) {
-          h = b[j];
-          ac = a[j];
-        } else {
-          h = fmaf(a[j], h, b[j]);
-          ac *= a[j];
+      for (int j = 0; j < kPerThread; ++j) {
+        b[j] = fmaf(a[j], P.b, b[j]);
+        if constexpr (GATES_OUT) a[j] *= P.a;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j) {
+        if ((cm >> j) & 1u) {
+          b[j] = fmaf(a[j], P.b, b[j]);
+          if constexpr (GATES_OUT) a[j] *= P.a;
         }
-        y[j] = h;
-        gp[j] = ac;
       }
     }
-    uint32_t valid = 0u;
-#pragma unroll
-    for (int j = 0; j < kPerThread; ++j)
-      if (o + j < n_valid) valid |= 1u << j;
-    valid &= ~omask;
+    const uint32_t valid = below_mask(o, n_valid) & ~omask;
     uint32_t direct = valid;
-    if (!has_outside) {
-      write_block<T>(sm.out[obuf][0], o, y);
-      if constexpr (GATES_OUT) write_block<T>(sm.out[obuf][1], o, gp);
-      uint32_t below_tma = 0u;
-#pragma unroll
-      for (int j = 0; j < kPerThread; ++j)
-        if (o + j < n_tma) below_tma |= 1u << j;
-      direct &= ~below_tma;
+    if (lane == 0) bulk_wait_read<1>();  // this warp's slice of staging buffer obuf is free
+    __syncwarp();
+    // this warp's slice goes out by TMA when it lies wholly inside the tile's
+    // TMA-covered part (never past a row end or the array end)
+    const bool slice_tma = !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
+    if (slice_tma) {
+      write_block<T>(sm.out[obuf][0], tc, b);
+      if constexpr (GATES_OUT) write_block<T>(sm.out[obuf][1], tc, a);
+      direct = 0u;
     }
     if (direct) {
-      store_direct<T>(args.y, p0 + o, direct, y);
-      if constexpr (GATES_OUT) store_direct<T>(args.gout, p0 + o, direct, gp);
+      store_direct<T>(args.y, p0 + o, direct, b);
+      if constexpr (GATES_OUT) store_direct<T>(args.gout, p0 + o, direct, a);
     }
     fence_async_smem();
-    consumer_sync();
-    if (tid == 0) {
-      if (!has_outside && n_tma > 0) {
-        const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow);
-        tma_store_2d(&map_y, 0, row, sm.out[obuf][0]);
-        if constexpr (GATES_OUT) tma_store_2d(&map_gout, 0, row, sm.out[obuf][1]);
+    __syncwarp();
+    if (lane == 0) {
+      if (slice_tma) {
+        const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow) + warp * kPartRows;
+        tma_store_2d(&map_y, 0, row, sm.out[obuf][0] + warp * kPartBytes);
+        if constexpr (GATES_OUT) tma_store_2d(&map_gout, 0, row, sm.out[obuf][1] + warp * kPartBytes);
       }
       bulk_commit();
     }
     obuf ^= 1u;
+    if (++xi == kXsRing) xi = 0;
   }
-  if (tid == 0) bulk_wait_all();
+  if (!ok && lane == 0) {
+    *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+    report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull);
+    set_aborted(args.st);
+  }
+  if (lane == 0) bulk_wait_all();
 }
 
 template <typename T, typename IdxT, bool CAUSAL, int NS>
@@ -657,7 +666,7 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
                         const __grid_constant__ CUtensorMap map_h,
                         const __grid_constant__ CUtensorMap map_dx,
                         const __grid_constant__ CUtensorMap map_dg, const BwdArgs<T, IdxT> args,
-                        int64_t n_tma_total) {
+                        int64_t n_tma_total, const tma::TileSched sch) {
   using namespace tma;
   constexpr bool REV = CAUSAL;
   constexpr int NIN = 3, NOUT = 2;
@@ -669,11 +678,16 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
   const bool cache_cu = (S + 1) <= kCuCache;
   if (cache_cu)
     for (int64_t i = tid; i <= S; i += tma::kThreads) sm.cu[i] = cu_at(args.cu, i, BL);
+  if (tid < kXsRing * (kConsumerWarps + 1)) {
+    float4* f = &sm.xs[0].warp[0] + tid;
+    f->w = __uint_as_float(kNoTag);
+  }
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kConsumerWarps);
     }
+    sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -682,22 +696,41 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
   if (warp == kConsumerWarps) {
     const CUtensorMap* maps[NIN] = {&map_dy, &map_g, &map_h};
     run_producer<T, IdxT, REV, NIN, NOUT, NS>(
-        sm, maps, cu, N, n_tma_total, args.num_tiles, args.ticket, args.st, lane,
-        [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln) {
+        sm, maps, cu, N, n_tma_total, sch, args.st, lane,
+        [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
+            uint64_t* bar) {
           for (uint32_t e = n_tma + ln; e < n_valid; e += 32) {
             m.tail[0][e - n_tma] = Cvt<T>::to(args.dy[p0 + e]);
             m.tail[1][e - n_tma] = Cvt<T>::to(args.g[p0 + e]);
             m.tail[2][e - n_tma] = Cvt<T>::to(args.h[p0 + e]);
           }
           if (ln == 0) {
-            const int64_t pn = p0 + kTileElems, pp = p0 - 1;
-            if (CAUSAL) {
-              m.halo[0] = pn < N ? Cvt<T>::to(args.g[pn]) : 1.f;
-              m.halo[1] = pp >= 0 ? Cvt<T>::to(args.h[pp]) : 0.f;
+            // The element after the tile (gate for the causal adjoint, state
+            // otherwise) and the one before it (the other array) come by
+            // 16-byte bulk copies, so the producer never waits for them: tile
+            // starts are 16-byte aligned, and so are the blocks [pn, pn+V) and
+            // [p0-V, p0).  A next block that would reach past the array end
+            // is read directly (the array's last tile only).
+            constexpr int V = 16 / static_cast<int>(sizeof(T));
+            const int64_t pn = p0 + kTileElems;
+            const int kn = CAUSAL ? 0 : 1, kp = CAUSAL ? 1 : 0;  // halo slots
+            const T* const arr[2] = {args.g, args.h};
+            const float ident[2] = {1.f, 0.f};
+            uint32_t bulk = 0u;
+            if (pn + V <= N) {
+              bulk |= 1u << kn;
             } else {
-              m.halo[0] = pp >= 0 ? Cvt<T>::to(args.g[pp]) : 1.f;
-              m.halo[1] = pn < N ? Cvt<T>::to(args.h[pn]) : 0.f;
+              m.halo[kn] = pn < N ? Cvt<T>::to(arr[kn][pn]) : ident[kn];
             }
+            if (p0 >= V) {
+              bulk |= 1u << kp;
+            } else {
+              m.halo[kp] = p0 > 0 ? Cvt<T>::to(arr[kp][p0 - 1]) : ident[kp];
+            }
+            m.halo_bulk = bulk;
+            if (bulk) mbar_expect_tx(bar, 16u * static_cast<uint32_t>(__popc(bulk)));
+            if (bulk & (1u << kn)) bulk_load(m.halo_raw[kn], arr[kn] + pn, 16u, bar);
+            if (bulk & (1u << kp)) bulk_load(m.halo_raw[kp], arr[kp] + (p0 - V), 16u, bar);
           }
         });
     return;
@@ -705,15 +738,16 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
 
   if (blockIdx.x == 0) validate_cu(args.cu, S, BL);
   const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
-  uint32_t stage = 0, phase = 0, obuf = 0;
-  while (true) {
-    // Leave only together: a timed-out wait is agreed on by every consumer.
-    const bool got = mbar_wait(&sm.full[stage], phase);
-    if (consumers_any(!got)) {
-      if (tid == 0) {
-        report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull);
-        set_aborted(args.st);
-      }
+  const ThreadChunks<T> tc(o);
+  const uint32_t bit_word = o >> 5, bit_shift = o & 31u;
+  constexpr int kPartRows = Fmt<T>::kRows / kConsumerWarps;    // this warp's slice of a tile
+  constexpr int kPartBytes = Fmt<T>::kBytes / kConsumerWarps;
+  uint32_t stage = 0, phase = 0, obuf = 0, xi = 0;
+  bool ok = true;
+  while (ok) {
+    const bool got = __all_sync(kFull, mbar_wait(&sm.full[stage], phase));
+    if (!got || *reinterpret_cast<volatile int*>(&sm.abort)) {
+      ok = false;
       break;
     }
     const StageMeta<NIN, T>& m = sm.meta[stage];
@@ -723,30 +757,36 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
     const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
     const bool has_outside = m.has_outside != 0u;
     float dyv[kPerThread], gv[kPerThread], hv[kPerThread];
-    read_block<T, NIN>(sm.in[stage][0], m, 0, o, n_tma, n_valid, 0.f, dyv);
-    read_block<T, NIN>(sm.in[stage][1], m, 1, o, n_tma, n_valid, 1.f, gv);
-    read_block<T, NIN>(sm.in[stage][2], m, 2, o, n_tma, n_valid, 0.f, hv);
+    read_block<T, NIN>(sm.in[stage][0], tc, m, 0, o, n_tma, n_valid, 0.f, dyv);
+    read_block<T, NIN>(sm.in[stage][1], tc, m, 1, o, n_tma, n_valid, 1.f, gv);
+    read_block<T, NIN>(sm.in[stage][2], tc, m, 2, o, n_tma, n_valid, 0.f, hv);
     // neighbours across the thread boundary: from the tile, or the tile-edge halo
+    constexpr int V = 16 / static_cast<int>(sizeof(T));
+    const float halo_g = (m.halo_bulk & 1u) ? Cvt<T>::to(m.halo_raw[0][CAUSAL ? 0 : V - 1])
+                                            : m.halo[0];
+    const float halo_h = (m.halo_bulk & 2u) ? Cvt<T>::to(m.halo_raw[1][CAUSAL ? V - 1 : 0])
+                                            : m.halo[1];
     float g_nb, h_nb;
     if (CAUSAL) {
       g_nb = (o + kPerThread < static_cast<uint32_t>(kTileElems))
                  ? tile_elem<T, NIN>(sm.in[stage][1], m, 1, o + kPerThread, n_tma, n_valid, 1.f)
-                 : m.halo[0];
+                 : halo_g;
       h_nb = (o > 0) ? tile_elem<T, NIN>(sm.in[stage][2], m, 2, o - 1, n_tma, n_valid, 0.f)
-                     : m.halo[1];
+                     : halo_h;
     } else {
       g_nb = (o > 0) ? tile_elem<T, NIN>(sm.in[stage][1], m, 1, o - 1, n_tma, n_valid, 1.f)
-                     : m.halo[0];
+                     : halo_g;
       h_nb = (o + kPerThread < static_cast<uint32_t>(kTileElems))
                  ? tile_elem<T, NIN>(sm.in[stage][2], m, 2, o + kPerThread, n_tma, n_valid, 0.f)
-                 : m.halo[1];
+                 : halo_h;
     }
-    const uint32_t sh = o & 31u;
-    const uint32_t smask = (m.sbits[o >> 5] >> sh) & 0xffffu;
-    const uint32_t emask = (m.ebits[o >> 5] >> sh) & 0xffffu;
-    const uint32_t omask = has_outside ? (m.obits[o >> 5] >> sh) & 0xffffu : 0u;
+    const uint32_t smask = (m.sbits[bit_word] >> bit_shift) & 0xffffu;
+    const uint32_t emask = (m.ebits[bit_word] >> bit_shift) & 0xffffu;
+    const uint32_t omask = has_outside ? (m.obits[bit_word] >> bit_shift) & 0xffffu : 0u;
     const bool first_is_head =
         REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
+    const bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
+    const Pfx te_meta{__uint_as_float(m.te_raw[0]), __uint_as_float(m.te_raw[2]), kValid};
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[stage]);
     if (++stage == NS) {
@@ -773,53 +813,52 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
     const uint32_t head = CAUSAL ? emask : smask;
     const uint32_t tail = CAUSAL ? smask : emask;
     Pfx ex, wtot;
-    warp_scan<REV>(fold16<REV>(gv, dyv, head), lane, ex, wtot);
-    if (tid == 0) bulk_wait_read<1>();
-    const Pfx P = consumer_tile_prefix<REV>(sm, ex, wtot, first_is_head, ticket, args.st, warp,
-                                            lane);
-    float dxo[kPerThread], dgo[kPerThread];
-    {
-      float d = P.b;
+    warp_scan<REV>(fold16_inplace<REV>(gv, dyv, head), lane, ex, wtot);
+    const Pfx P = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
+                                        sch.stride, te_known, te_meta, warp, lane, ok);
+    // gv, dyv hold the local prefixes: dh = A_loc * carry + B_loc before the first head
+    const uint32_t cm = carry_mask<REV>(head);
 #pragma unroll
-      for (int jj = 0; jj < kPerThread; ++jj) {
-        const int j = REV ? kPerThread - 1 - jj : jj;
-        d = ((head >> j) & 1u) ? dyv[j] : fmaf(gv[j], d, dyv[j]);
-        dxo[j] = d;
-        dgo[j] = ((tail >> j) & 1u) ? 0.f : d * hv[j];
-      }
+    for (int j = 0; j < kPerThread; ++j) {
+      const float d = ((cm >> j) & 1u) ? fmaf(gv[j], P.b, dyv[j]) : dyv[j];
+      dyv[j] = d;                                    // dx
+      gv[j] = ((tail >> j) & 1u) ? 0.f : d * hv[j];  // dg
     }
-    uint32_t valid = 0u;
-#pragma unroll
-    for (int j = 0; j < kPerThread; ++j)
-      if (o + j < n_valid) valid |= 1u << j;
-    valid &= ~omask;
+    const uint32_t valid = below_mask(o, n_valid) & ~omask;
     uint32_t direct = valid;
-    if (!has_outside) {
-      write_block<T>(sm.out[obuf][0], o, dxo);
-      write_block<T>(sm.out[obuf][1], o, dgo);
-      uint32_t below_tma = 0u;
-#pragma unroll
-      for (int j = 0; j < kPerThread; ++j)
-        if (o + j < n_tma) below_tma |= 1u << j;
-      direct &= ~below_tma;
+    if (lane == 0) bulk_wait_read<1>();  // this warp's slice of staging buffer obuf is free
+    __syncwarp();
+    // this warp's slice goes out by TMA when it lies wholly inside the tile's
+    // TMA-covered part (never past a row end or the array end)
+    const bool slice_tma = !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
+    if (slice_tma) {
+      write_block<T>(sm.out[obuf][0], tc, dyv);
+      write_block<T>(sm.out[obuf][1], tc, gv);
+      direct = 0u;
     }
     if (direct) {
-      store_direct<T>(args.dx, p0 + o, direct, dxo);
-      store_direct<T>(args.dg, p0 + o, direct, dgo);
+      store_direct<T>(args.dx, p0 + o, direct, dyv);
+      store_direct<T>(args.dg, p0 + o, direct, gv);
     }
     fence_async_smem();
-    consumer_sync();
-    if (tid == 0) {
-      if (!has_outside && n_tma > 0) {
-        const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow);
-        tma_store_2d(&map_dx, 0, row, sm.out[obuf][0]);
-        tma_store_2d(&map_dg, 0, row, sm.out[obuf][1]);
+    __syncwarp();
+    if (lane == 0) {
+      if (slice_tma) {
+        const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow) + warp * kPartRows;
+        tma_store_2d(&map_dx, 0, row, sm.out[obuf][0] + warp * kPartBytes);
+        tma_store_2d(&map_dg, 0, row, sm.out[obuf][1] + warp * kPartBytes);
       }
       bulk_commit();
     }
     obuf ^= 1u;
+    if (++xi == kXsRing) xi = 0;
   }
-  if (tid == 0) bulk_wait_all();
+  if (!ok && lane == 0) {
+    *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+    report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull);
+    set_aborted(args.st);
+  }
+  if (lane == 0) bulk_wait_all();
 }
 
 // ---------------------------------------------------------------------------
@@ -878,21 +917,19 @@ static size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255);
 
 static size_t tiles_of(int64_t n) { return static_cast<size_t>((n + kTile - 1) / kTile); }
 
-static size_t workspace_bytes_for(int64_t n) {
-  const size_t tiles = tiles_of(n);
-  return 256 + align256(tiles * sizeof(uint32_t)) + tiles * sizeof(float4);
-}
+// 256-byte header (ticket counter, abort word) + one 16-byte status slot per tile.
+static size_t workspace_bytes_for(int64_t n) { return 256 + tiles_of(n) * sizeof(uint4); }
 
 static int carve(void* ws, size_t ws_bytes, int64_t n, Workspace& out) {
   if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return ASCAN_EWORKSPACE;
   if (ws_bytes < workspace_bytes_for(n)) return ASCAN_EWORKSPACE;
   char* base = static_cast<char*>(ws);
   const size_t tiles = tiles_of(n);
+  (void)tiles;
   out.ticket = reinterpret_cast<uint32_t*>(base);
   out.st.abort = reinterpret_cast<uint32_t*>(base + 4);
-  out.st.flags = reinterpret_cast<uint32_t*>(base + 256);
-  out.st.vals = reinterpret_cast<float4*>(base + 256 + align256(tiles * sizeof(uint32_t)));
-  out.clear_bytes = 256 + align256(tiles * sizeof(uint32_t));
+  out.st.slots = reinterpret_cast<uint4*>(base + 256);
+  out.clear_bytes = 256 + tiles * sizeof(uint4);
   return ASCAN_OK;
 }
 
@@ -909,17 +946,26 @@ static int launch_status() {
 
 // ---- implementation choice ------------------------------------------------
 
-// 0: automatic (TMA kernels when the pointers and sizes allow), 1: always the
-// plain kernels, 2: TMA kernels whenever possible (same as 0 today).
+// 0: automatic (the TMA kernels whenever possible, automatic tile order),
+// 1: always the plain kernels, 2: TMA kernels whenever possible with the
+// automatic tile order (same as 0), 3: TMA kernels with tiles in flat
+// order, 4: TMA kernels with row order whenever rows are tile-aligned.
+// ASCAN_IMPL=simple|tma|tma-flat|tma-row selects 1..4 at first use.
 static int g_impl = -1;
 
 static int impl_mode() {
   if (g_impl < 0) {
     const char* e = getenv("ASCAN_IMPL");
-    g_impl = (e && strcmp(e, "simple") == 0) ? 1 : (e && strcmp(e, "tma") == 0) ? 2 : 0;
+    g_impl = 0;
+    if (e && strcmp(e, "simple") == 0) g_impl = 1;
+    if (e && strcmp(e, "tma") == 0) g_impl = 2;
+    if (e && strcmp(e, "tma-flat") == 0) g_impl = 3;
+    if (e && strcmp(e, "tma-row") == 0) g_impl = 4;
   }
   return g_impl;
 }
+
+static bool use_tma() { return impl_mode() != 1; }
 
 // ---- TMA descriptors -------------------------------------------------------
 
@@ -940,7 +986,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // The flat array seen as `rows` rows of 128 bytes; one box = one 4096-element
 // tile, stored in shared memory with the 128-byte swizzle.
 template <typename T>
-static bool make_map(CUtensorMap* m, const void* base, int64_t rows) {
+static bool make_map(CUtensorMap* m, const void* base, int64_t rows,
+                     int box_rows = tma::Fmt<T>::kRows) {
   const auto fn = encode_fn();
   if (!fn || rows <= 0 || rows > 0x7fffffffll) return false;
   const CUtensorMapDataType dt =
@@ -951,7 +998,7 @@ static bool make_map(CUtensorMap* m, const void* base, int64_t rows) {
                               static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {128};
   const cuuint32_t box[2] = {static_cast<cuuint32_t>(tma::Fmt<T>::kElemsPerRow),
-                             static_cast<cuuint32_t>(tma::Fmt<T>::kRows)};
+                             static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -965,6 +1012,65 @@ static int sm_count() {
   return n;
 }
 
+// Cooperative launch of a persistent TMA kernel: one CTA per SM that can hold
+// it (never more CTAs than tiles).  Co-residency of every CTA is what makes the
+// round-robin tile schedule safe.  1: launched, 0: not possible here (the
+// caller falls back to the plain kernel), <0: error.
+static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles, void** params,
+                              cudaStream_t s) {
+  const int sms = sm_count();
+  if (sms <= 0) return 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return ASCAN_ECUDA;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tma::kThreads, smem) !=
+          cudaSuccess ||
+      per_sm <= 0)
+    return 0;
+  const uint32_t resident = static_cast<uint32_t>(sms) * static_cast<uint32_t>(per_sm);
+  const uint32_t grid = num_tiles < resident ? num_tiles : resident;
+  const cudaError_t e =
+      cudaLaunchCooperativeKernel(kern, dim3(grid), dim3(tma::kThreads), params, smem, s);
+  if (e != cudaSuccess) {
+    fprintf(stderr, "ascan: cooperative launch failed: %s\n", cudaGetErrorString(e));
+    cudaGetLastError();
+    return ASCAN_ECUDA;
+  }
+  return 1;
+}
+
+// Tile order for a persistent launch.  Row mode needs rows that are whole
+// tiles (so the tile count -- and the workspace -- is that of the flat mode)
+// and at least two waves of rows, so that a tile's predecessor is old enough
+// to be read ahead.
+// Tile order of the TMA kernels: row mode needs row-aligned tiles (BL a
+// multiple of the tile) and pays off when sequences span several tiles (in
+// flat order their tiles are consecutive tickets of one wave, so every tile
+// waits for the one before it) and a tile's row predecessor is at least two
+// waves older (rows >= 2 x CTAs).  When sequences fit in a tile on average,
+// the flat order is slightly faster (a wave reads one contiguous range).
+// Implementations 3 and 4 force the flat and the row order; both orders give
+// the same results up to floating-point reassociation.
+static tma::TileSched make_sched(uint32_t num_tiles, int64_t N, int64_t BL, int64_t S) {
+  tma::TileSched sch{num_tiles, 0u, 0u, 0u, 1u};
+  const int64_t C = BL > 0 ? N / BL : 0;
+  const int sms = sm_count();
+  const int mode = impl_mode();
+  const bool fits = BL % kTile == 0 && C >= 1 && C <= 0x7fffffffll;
+  const bool long_seqs = BL > S * static_cast<int64_t>(kTile);  // mean length above a tile
+  const bool row = mode == 4   ? fits
+                   : mode == 3 ? false
+                               : fits && long_seqs && sms > 0 && C >= 2ll * sms;
+  if (row) {
+    sch.row_mode = 1u;
+    sch.rows = static_cast<uint32_t>(C);
+    sch.tiles_per_row = static_cast<uint32_t>(BL / kTile);
+    sch.stride = static_cast<uint32_t>(C);
+  }
+  return sch;
+}
+
 // 1: launched, 0: not applicable (caller falls back to the plain kernel), <0: error
 template <typename T, typename IdxT, bool REV, bool GOUT>
 static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, cudaStream_t s) {
@@ -974,24 +1080,20 @@ static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, cudaStream_t s) {
   static_assert(smem <= kSmemBudget, "TMA forward ring does not fit in shared memory");
   const int64_t rows = a.N / tma::Fmt<T>::kElemsPerRow;
   CUtensorMap mg, mx, my, mgo;
+  constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;  // stores: one warp's slice
   if (!make_map<T>(&mg, a.g, rows) || !make_map<T>(&mx, a.x, rows) ||
-      !make_map<T>(&my, a.y, rows))
+      !make_map<T>(&my, a.y, rows, kPart))
     return 0;
   if (GOUT) {
-    if (!make_map<T>(&mgo, a.gout, rows)) return 0;
+    if (!make_map<T>(&mgo, a.gout, rows, kPart)) return 0;
   } else {
     mgo = my;
   }
-  const int sms = sm_count();
-  if (sms <= 0) return 0;
   auto kern = scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem)) != cudaSuccess)
-    return ASCAN_ECUDA;
-  const unsigned grid = a.num_tiles < static_cast<uint32_t>(sms) ? a.num_tiles : sms;
-  kern<<<grid, tma::kThreads, smem, s>>>(mg, mx, my, mgo, a,
-                                          rows * tma::Fmt<T>::kElemsPerRow);
-  return launch_status() == ASCAN_OK ? 1 : ASCAN_ECUDA;
+  int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
+  tma::TileSched sch = make_sched(a.num_tiles, a.N, a.BL, a.S);
+  void* params[] = {&mg, &mx, &my, &mgo, const_cast<FwdArgs<T, IdxT>*>(&a), &n_tma_total, &sch};
+  return launch_cooperative(reinterpret_cast<const void*>(kern), smem, a.num_tiles, params, s);
 }
 
 template <typename T, typename IdxT, bool CAUSAL>
@@ -1001,20 +1103,17 @@ static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, cudaStream_t s) {
   static_assert(smem <= kSmemBudget, "TMA backward ring does not fit in shared memory");
   const int64_t rows = a.N / tma::Fmt<T>::kElemsPerRow;
   CUtensorMap mdy, mg, mh, mdx, mdg;
+  constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;  // stores: one warp's slice
   if (!make_map<T>(&mdy, a.dy, rows) || !make_map<T>(&mg, a.g, rows) ||
-      !make_map<T>(&mh, a.h, rows) || !make_map<T>(&mdx, a.dx, rows) ||
-      !make_map<T>(&mdg, a.dg, rows))
+      !make_map<T>(&mh, a.h, rows) || !make_map<T>(&mdx, a.dx, rows, kPart) ||
+      !make_map<T>(&mdg, a.dg, rows, kPart))
     return 0;
-  const int sms = sm_count();
-  if (sms <= 0) return 0;
   auto kern = scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem)) != cudaSuccess)
-    return ASCAN_ECUDA;
-  const unsigned grid = a.num_tiles < static_cast<uint32_t>(sms) ? a.num_tiles : sms;
-  kern<<<grid, tma::kThreads, smem, s>>>(mdy, mg, mh, mdx, mdg, a,
-                                          rows * tma::Fmt<T>::kElemsPerRow);
-  return launch_status() == ASCAN_OK ? 1 : ASCAN_ECUDA;
+  int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
+  tma::TileSched sch = make_sched(a.num_tiles, a.N, a.BL, a.S);
+  void* params[] = {&mdy, &mg, &mh, &mdx, &mdg, const_cast<BwdArgs<T, IdxT>*>(&a), &n_tma_total,
+                    &sch};
+  return launch_cooperative(reinterpret_cast<const void*>(kern), smem, a.num_tiles, params, s);
 }
 
 template <typename T, typename IdxT, int VEC>
@@ -1051,7 +1150,7 @@ static int fwd_typed(const void* g, const void* x, void* y, void* gout, const vo
   a.st = w.st;
   const bool vec = aligned16(g) && aligned16(x) && aligned16(y) && (!gout || aligned16(gout));
   constexpr int kVec = 16 / sizeof(T);
-  if (vec && impl_mode() == 2 && a.N >= tma::Fmt<T>::kElemsPerRow) {
+  if (vec && use_tma() && a.N >= tma::Fmt<T>::kElemsPerRow) {
     int rc;
     if (reverse)
       rc = gout ? launch_fwd_tma<T, IdxT, true, true>(a, s) : launch_fwd_tma<T, IdxT, true, false>(a, s);
@@ -1094,7 +1193,7 @@ static int bwd_typed(const void* dy, const void* g, const void* h, void* dx, voi
   a.st = w.st;
   const bool vec = aligned16(dy) && aligned16(g) && aligned16(h) && aligned16(dx) && aligned16(dg);
   constexpr int kVec = 16 / sizeof(T);
-  if (vec && impl_mode() == 2 && a.N >= tma::Fmt<T>::kElemsPerRow) {
+  if (vec && use_tma() && a.N >= tma::Fmt<T>::kElemsPerRow) {
     const int rc = causal ? launch_bwd_tma<T, IdxT, true>(a, s) : launch_bwd_tma<T, IdxT, false>(a, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
   }
@@ -1130,6 +1229,7 @@ static int check_common(const void* cu, int cu_type, int64_t S, int64_t C, int64
 }  // namespace ascan
 
 using namespace ascan;
+
 
 extern "C" {
 
@@ -1287,7 +1387,7 @@ int ascan_forward_noalloc(const void* gates, const void* tokens, void* tokens_ou
 }
 
 int ascan_set_implementation(int impl) {
-  if (impl < 0 || impl > 2) return ASCAN_EINVAL;
+  if (impl < 0 || impl > 4) return ASCAN_EINVAL;
   g_impl = impl;
   return ASCAN_OK;
 }

@@ -359,39 +359,23 @@ __device__ __forceinline__ void warp_scan(Pfx v, int lane, Pfx& excl, Pfx& total
 // Prefix Scan with Decoupled Look-back", 2016), indexed by dynamic ticket.
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ float2 ld_relaxed_f2(const float* p) {
-  float2 v;
-  asm volatile("ld.relaxed.gpu.global.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_relaxed_f2(float* p, float a, float b) {
-  asm volatile("st.relaxed.gpu.global.v2.f32 [%0], {%1,%2};" ::"l"(p), "f"(a), "f"(b) : "memory");
-}
-
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
 
-// Status slot of a ticket: flag word plus (aggregate a, b, inclusive a, b).
-// `abort` is a per-launch word: once any wait of the launch has given up, every
-// other wait returns at once, so a lost predecessor costs one timeout, not one
-// per tile.
+// Tile status records, one 16-byte slot per ticket: two 64-bit words
+// {a, state} and {b, state} written by one relaxed vector store.  Each
+// aligned 64-bit word is single-copy atomic, states only grow
+// (none -> aggregate -> inclusive), and a reader accepts a slot only when
+// both words carry the same state -- so no fence orders the value before the
+// flag, and publishing never stalls the publishing warp.
+// `abort` is a per-launch word: once any wait of the launch has given up,
+// every other wait returns at once, so a lost predecessor costs one timeout,
+// not one per tile.
 struct TileStatus {
-  uint32_t* flags;
-  float4* vals;
+  uint4* slots;
   uint32_t* abort;
 };
 
@@ -409,22 +393,36 @@ __device__ __forceinline__ void set_aborted(const TileStatus& st) { atomicExch(s
 
 __device__ __forceinline__ void publish(const TileStatus& st, uint32_t ticket, uint32_t kind,
                                         float a, float b) {
-  float* dst = reinterpret_cast<float*>(st.vals + ticket) + (kind == kStatusInclusive ? 2 : 0);
-  st_relaxed_f2(dst, a, b);
-  st_release(st.flags + ticket, kind);
+  asm volatile("st.relaxed.gpu.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(st.slots + ticket),
+               "r"(__float_as_uint(a)), "r"(kind), "r"(__float_as_uint(b)), "r"(kind)
+               : "memory");
 }
 
-// Wait (bounded) until the status of `ticket` is published; 0 on timeout or
-// when the launch has been aborted.
-__device__ __forceinline__ uint32_t wait_status(const TileStatus& st, uint32_t ticket) {
-  uint32_t s = ld_acquire(st.flags + ticket);
+// One read of a slot; returns its state (kStatusNone when empty or torn).
+__device__ __forceinline__ uint32_t read_status(const TileStatus& st, uint32_t ticket, float& a,
+                                                float& b) {
+  uint32_t w0, w1, w2, w3;
+  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+               : "l"(st.slots + ticket)
+               : "memory");
+  a = __uint_as_float(w0);
+  b = __uint_as_float(w2);
+  return (w1 == w3) ? w1 : kStatusNone;
+}
+
+// Wait (bounded) until the status of `ticket` is published; kStatusNone on
+// timeout or when the launch has been aborted.
+__device__ __forceinline__ uint32_t wait_status(const TileStatus& st, uint32_t ticket, float& a,
+                                                float& b) {
+  uint32_t s = read_status(st, ticket, a, b);
   if (s != kStatusNone) return s;
   const unsigned long long t0 = globaltimer();
   unsigned ns = 16;
   while (true) {
     __nanosleep(ns);
     if (ns < 256) ns <<= 1;
-    s = ld_acquire(st.flags + ticket);
+    s = read_status(st, ticket, a, b);
     if (s != kStatusNone) return s;
     if (launch_aborted(st)) return kStatusNone;
     if (globaltimer() - t0 > kLookbackTimeoutNs) {
@@ -433,5 +431,96 @@ __device__ __forceinline__ uint32_t wait_status(const TileStatus& st, uint32_t t
     }
   }
 }
+
+// Warp-parallel decoupled look-back (all 32 lanes).  The window covers the
+// 32*K tiles before `ticket` in scan order, whose tickets are `stride` apart
+// (1 when tiles follow each other in the flat array, the number of rows when
+// they are dealt tile-major across rows): lane l owns the K consecutive
+// predecessors at distance K*l+1 .. K*l+K (slot i = 0 is the nearest).  Each
+// poll reads the whole window in one round trip, finds the nearest inclusive
+// record and is satisfied once every slot nearer than it holds at least an
+// aggregate -- slots beyond it are never waited for.  A window without an
+// inclusive record is composed whole and the window slides back.  Returns the
+// exclusive prefix of `ticket`; *timed_out is set when a needed predecessor
+// was not published within the bounded wait (it then counts as empty).
+template <int K>
+__device__ __forceinline__ Pfx lookback_warp(const TileStatus& st, uint32_t ticket, int lane,
+                                             bool* timed_out, uint32_t stride = 1u) {
+  Pfx te = pfx_empty();
+  int64_t base = 0;  // distance (in predecessors) of this window's nearest slot, minus one
+  bool lost = false;
+  while (true) {
+    uint32_t sk[K];
+    float va[K], vb[K];
+    int my_inc = K;   // nearest inclusive slot of this lane (K: none)
+    int stop = 32;    // first lane holding an inclusive slot (32: none)
+    unsigned long long t0 = 0;
+    unsigned ns = 16;
+    for (int poll = 0;; ++poll) {
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        const int64_t q = static_cast<int64_t>(ticket) -
+                          (base + static_cast<int64_t>(K) * lane + i + 1) * stride;
+        if (q < 0) {
+          sk[i] = kStatusInclusive;  // nothing precedes ticket 0: a zero state
+          va[i] = 1.f;
+          vb[i] = 0.f;
+        } else {
+          sk[i] = read_status(st, static_cast<uint32_t>(q), va[i], vb[i]);
+        }
+      }
+      my_inc = K;
+#pragma unroll
+      for (int i = K - 1; i >= 0; --i)
+        if (sk[i] == kStatusInclusive) my_inc = i;
+      const unsigned incmask = __ballot_sync(kFull, my_inc < K);
+      stop = incmask ? (__ffs(incmask) - 1) : 32;
+      bool missing = false;
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        const bool needed = lane < stop || (lane == stop && i < my_inc);
+        if (needed && sk[i] == kStatusNone) missing = true;
+      }
+      if (!__any_sync(kFull, missing)) break;
+      if (poll == 0) t0 = globaltimer();
+      __nanosleep(ns);
+      if (ns < 256) ns <<= 1;
+      const bool give_up = launch_aborted(st) || (globaltimer() - t0 > kLookbackTimeoutNs);
+      if (__any_sync(kFull, give_up)) {
+        if (lane == 0) set_aborted(st);
+        lost = true;  // unpublished slots count as empty records
+        break;
+      }
+    }
+    Pfx x = pfx_empty();
+    if (lane <= stop) {
+#pragma unroll
+      for (int i = K - 1; i >= 0; --i) {  // earliest first
+        if (lane == stop && i > my_inc) continue;
+        if (sk[i] == kStatusInclusive)
+          x = Pfx{va[i], vb[i], kValid | kHead};
+        else if (sk[i] == kStatusAggregate)
+          x = compose(x, Pfx{va[i], vb[i], kValid});
+      }
+    }
+    // x_31 o ... o x_1 o x_0 (a higher lane holds earlier tiles)
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const Pfx o{__shfl_down_sync(kFull, x.a, off), __shfl_down_sync(kFull, x.b, off),
+                  __shfl_down_sync(kFull, x.f, off)};
+      if (lane + off < 32) x = compose(o, x);
+    }
+    const Pfx part{__shfl_sync(kFull, x.a, 0), __shfl_sync(kFull, x.b, 0),
+                   __shfl_sync(kFull, x.f, 0)};
+    te = compose(part, te);
+    if (stop < 32 || lost) break;
+    base += 32 * K;
+  }
+  *timed_out = __any_sync(kFull, lost);
+  te.f &= ~kHead;
+  return te;
+}
+
+constexpr int kLookbackPerLane = 8;  // window of 256 predecessors per round trip
 
 }  // namespace ascan

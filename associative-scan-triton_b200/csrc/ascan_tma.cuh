@@ -15,10 +15,12 @@
 // streaming the next stages while a tile is computed or waits on a
 // predecessor.
 //
-// Every wait is bounded: mbarrier waits and look-back polls give up after
-// kLookbackTimeoutNs, report ASCAN_DEV_ERR_LOOKBACK and set the launch's abort
-// word, after which no wait of the launch blocks again.  Consumers leave their
-// loop only together (a bar.red vote), never one warp alone.
+// There is no CTA-wide barrier after the prologue: consumer warps hand their
+// per-tile totals to each other through tagged shared-memory slots and store
+// their own slice of each tile.  Every wait is bounded: mbarrier waits, slot
+// waits and look-back polls give up after kLookbackTimeoutNs, report
+// ASCAN_DEV_ERR_LOOKBACK and set the CTA's and the launch's abort words, after
+// which no wait blocks again.
 #pragma once
 
 #include <cuda.h>
@@ -37,8 +39,6 @@ static_assert(kTileElems == kTile, "TMA and plain kernels share the tile size");
 constexpr int kBitWords = kTileElems / 32;       // 128
 constexpr int kCuCache = 1024;                   // cu_seqlens entries cached in smem
 constexpr uint32_t kDone = 0xffffffffu;
-constexpr int kNamedBarrier = 1;   // consumer-only bar.sync
-constexpr int kAgreeBarrier = 2;   // consumer-only bar.red
 
 template <typename T>
 struct Fmt {
@@ -113,6 +113,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a
+// multiple of 16), completing on the same mbarrier as the tile loads.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
+      "r"(smem_addr(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y,
                                              const void* src) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
@@ -137,24 +148,6 @@ __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void consumer_sync() {
-  asm volatile("bar.sync %0, %1;" ::"n"(kNamedBarrier), "n"(kConsumers) : "memory");
-}
-
-// OR of `pred` over the 256 consumer threads (all of them must call it).
-__device__ __forceinline__ bool consumers_any(bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 q, %1, 0;\n\t"
-      "bar.red.or.pred p, %2, %3, q;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(pred)), "n"(kAgreeBarrier), "n"(kConsumers)
-      : "memory");
-  return r != 0u;
-}
-
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -171,10 +164,46 @@ struct StageMeta {
   uint32_t has_outside;
   int64_t p0;          // flat index of the tile's first element
   float halo[2];       // bwd: [0] gate neighbour, [1] state neighbour at the tile edge
+  uint32_t halo_bulk;  // bit k: halo k is in halo_raw[k] instead of halo[k]
+  // bwd: the 16-byte block holding halo k, fetched by a bulk copy with the tile
+  // (the block starting at the element after the tile, or ending at the
+  // element before it)
+  alignas(16) T halo_raw[2][16 / sizeof(T)];
+  // row mode: copy of the predecessor's 16-byte status slot, fetched by a bulk
+  // copy together with the tile (all zero = unknown); an inclusive record in
+  // it is the tile's carry-in
+  alignas(16) uint32_t te_raw[4];
   alignas(16) uint32_t sbits[kBitWords];  // sequence starts (and positions outside any sequence)
   alignas(16) uint32_t ebits[kBitWords];  // sequence ends   (and positions outside any sequence)
   alignas(16) uint32_t obits[kBitWords];  // positions outside any sequence (valid if has_outside)
   float tail[NIN][Fmt<T>::kTailMax];
+};
+
+// Order in which tiles are dealt (as tickets, i.e. in scan order).
+//  flat mode: tile k of the flat [C*BL] array is ticket k (reverse scans count
+//             from the end); a tile's scan predecessor is ticket - 1.
+//  row mode:  every row is cut into row-aligned tiles and the tiles are dealt
+//             tile-major across rows (tile j of every row, then tile j+1), so
+//             a tile's predecessor in its row is ticket - rows: many waves
+//             old when rows >> CTAs, and its status can be read ahead.
+struct TileSched {
+  uint32_t num_tiles;
+  uint32_t row_mode;
+  uint32_t rows;            // row mode: C
+  uint32_t tiles_per_row;   // row mode: ceil(BL / kTileElems)
+  uint32_t stride;          // ticket distance to the scan predecessor
+};
+
+// Hand-off slots between the consumer warps of one tile (no CTA barrier): the
+// per-warp totals and the tile's carry-in, each tagged with the tile's
+// ticket.  Warps can drift apart by at most the ring depth (a stage is only
+// refilled once every warp has read it), so kXsRing > depth keeps slots apart.
+constexpr int kXsRing = 8;
+constexpr uint32_t kNoTag = 0xffffffffu;
+
+struct XSlot {
+  float4 warp[kConsumerWarps];  // {a, b, flags bits, ticket bits}
+  float4 te;                    // tile carry-in {a, b, flags bits, ticket bits}
 };
 
 template <int NIN, int NOUT, int NS, typename T>
@@ -185,9 +214,8 @@ struct Smem {
   uint64_t full[NS];
   uint64_t empty[NS];
   int64_t cu[kCuCache];
-  Pfx warp_total[kConsumerWarps];
-  Pfx te;
-  int abort;
+  XSlot xs[kXsRing];
+  int abort;  // a consumer warp gave up: the others stop waiting on it
 };
 
 template <int NIN, int NOUT, int NS, typename T>
@@ -228,86 +256,93 @@ struct CuView {
   }
 };
 
-// Bits [lo, hi) (lo, hi relative to a 128-bit span) into words w[0..3].
-__device__ __forceinline__ void set_range(uint32_t (&w)[4], uint32_t lo, uint32_t hi) {
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint32_t a = lo > 32u * k ? lo - 32u * k : 0u;
-    const uint32_t b = hi > 32u * k ? (hi - 32u * k < 32u ? hi - 32u * k : 32u) : 0u;
-    if (b > a) w[k] |= (b - a == 32u ? 0xffffffffu : ((1u << (b - a)) - 1u)) << a;
-  }
+__device__ __forceinline__ void or_bit(uint32_t* words, uint32_t e) {
+  atomicOr(&words[e >> 5], 1u << (e & 31));
 }
 
-__device__ __forceinline__ void set_one(uint32_t (&w)[4], uint32_t bit) {
-#pragma unroll
-  for (int k = 0; k < 4; ++k) w[k] |= (bit >> 5) == static_cast<uint32_t>(k) ? 1u << (bit & 31) : 0u;
-}
-
-// Boundaries of row positions [t, t+len), which sit at bit offset `pos` of
-// this lane's 128-element span: starts (cu[i], i < S), ends (cu[j]-1, j >= 1)
-// and positions before cu[0] (which belong to no sequence).
-template <typename IdxT>
-__device__ __forceinline__ void mark_span(uint32_t (&sw)[4], uint32_t (&ew)[4], uint32_t (&ow)[4],
-                                          const CuView<IdxT>& cu, int64_t t, int64_t len,
-                                          uint32_t pos) {
+// Marks, for row positions [t, t+len) sitting at tile offset `pos`, the
+// sequence starts (cu[i], i < S), the sequence ends (cu[j]-1, j >= 1) and the
+// positions before cu[0] (which belong to no sequence).  One binary search
+// per segment; the heads found are spread over the 32 lanes.
+template <typename IdxT, int NIN, typename T>
+__device__ __forceinline__ void mark_segment(StageMeta<NIN, T>& m, const CuView<IdxT>& cu,
+                                             int64_t t, int64_t len, uint32_t pos, int lane,
+                                             bool& outside) {
   const int64_t end = t + len;
   const int64_t cu0 = cu.at(0);
   if (cu0 > t) {
-    const uint32_t hi = pos + static_cast<uint32_t>((cu0 < end ? cu0 : end) - t);
-    set_range(sw, pos, hi);
-    set_range(ew, pos, hi);
-    set_range(ow, pos, hi);
+    const int64_t oend = cu0 < end ? cu0 : end;
+    for (int64_t q = t + lane; q < oend; q += 32) {
+      const uint32_t e = pos + static_cast<uint32_t>(q - t);
+      or_bit(m.sbits, e);
+      or_bit(m.ebits, e);
+      or_bit(m.obits, e);
+    }
+    outside = true;
   }
-  for (int64_t i = cu.lower_bound(0, cu.S, t); i < cu.S; ++i) {
-    const int64_t v = cu.at(i);
-    if (v >= end) break;
-    if (v >= t) set_one(sw, pos + static_cast<uint32_t>(v - t));
+  const int64_t i0 = cu.lower_bound(0, cu.S, t);
+  // starts cu[i] in [t, end) and ends cu[j]-1 in [t, end), both from i0 on
+  for (int64_t i = i0 + lane;; i += 32) {
+    bool any = false;
+    if (i < cu.S) {
+      const int64_t v = cu.at(i);
+      if (v < end) {
+        any = true;
+        if (v >= t) or_bit(m.sbits, pos + static_cast<uint32_t>(v - t));
+      }
+    }
+    if (!__any_sync(kFull, any)) break;
   }
-  for (int64_t j = cu.lower_bound(1, cu.S + 1, t + 1); j <= cu.S; ++j) {
-    const int64_t v = cu.at(j) - 1;
-    if (v >= end) break;
-    if (v >= t) set_one(ew, pos + static_cast<uint32_t>(v - t));
+  for (int64_t j = (i0 > 0 ? i0 : 1) + lane;; j += 32) {
+    bool any = false;
+    if (j <= cu.S) {
+      const int64_t v = cu.at(j) - 1;
+      if (v < end) {
+        any = true;
+        if (v >= t) or_bit(m.ebits, pos + static_cast<uint32_t>(v - t));
+      }
+    }
+    if (!__any_sync(kFull, any)) break;
   }
 }
 
-// Builds the boundary bitmaps of the tile that starts at flat index p0.  Lane
-// l owns tile elements [128 l, 128 l + 128) and writes its 4 words of each
-// bitmap once, without shared-memory atomics.  Called by all 32 lanes.
+// Builds the boundary bitmaps of the tile that starts at flat index p0, whose
+// first element sits at row position t0 and whose elements end at flat index
+// `limit` (the array end, or the row end in row mode).  Called by all lanes.
 template <typename IdxT, int NIN, typename T>
-__device__ void build_meta(StageMeta<NIN, T>& m, const CuView<IdxT>& cu, int64_t p0, int64_t N,
-                           int64_t n_tma_total, int lane) {
-  const int64_t rem = N - p0;
+__device__ void build_meta(StageMeta<NIN, T>& m, const CuView<IdxT>& cu, int64_t p0, int64_t t0,
+                           int64_t limit, int64_t n_tma_total, int lane) {
+  const int64_t rem = limit - p0;  // elements of the tile that belong to it (row or array end)
   const uint32_t n_valid = static_cast<uint32_t>(rem < kTileElems ? rem : kTileElems);
   int64_t nt = n_tma_total - p0;
   nt = nt < 0 ? 0 : (nt > n_valid ? n_valid : nt);
-  uint32_t sw[4] = {0u, 0u, 0u, 0u}, ew[4] = {0u, 0u, 0u, 0u}, ow[4] = {0u, 0u, 0u, 0u};
-  const uint32_t e0 = static_cast<uint32_t>(lane) * 128u;
-  const int64_t BL = cu.BL;
-  if (e0 < n_valid) {
-    const int64_t p = p0 + e0;
-    int64_t t = (p < 0xffffffffll && BL < 0xffffffffll)
-                    ? static_cast<int64_t>(static_cast<uint32_t>(p) % static_cast<uint32_t>(BL))
-                    : p % BL;
-    const uint32_t stop = (e0 + 128u < n_valid ? e0 + 128u : n_valid) - e0;
-    uint32_t pos = 0u;
-    while (pos < stop) {
-      int64_t len = static_cast<int64_t>(stop - pos);
-      if (len > BL - t) len = BL - t;
-      mark_span(sw, ew, ow, cu, t, len, pos);
-      pos += static_cast<uint32_t>(len);
-      t = 0;
-    }
-  }
   // positions past the end of the array are isolated and never stored
+  uint32_t past[4] = {0u, 0u, 0u, 0u};
+  const uint32_t e0 = static_cast<uint32_t>(lane) * 128u;
   if (n_valid < e0 + 128u) {
     const uint32_t lo = n_valid > e0 ? n_valid - e0 : 0u;
-    set_range(sw, lo, 128u);
-    set_range(ew, lo, 128u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t a = lo > 32u * k ? lo - 32u * k : 0u;
+      if (a < 32u) past[k] = 0xffffffffu << a;
+    }
   }
-  *reinterpret_cast<uint4*>(&m.sbits[lane * 4]) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
-  *reinterpret_cast<uint4*>(&m.ebits[lane * 4]) = make_uint4(ew[0], ew[1], ew[2], ew[3]);
-  *reinterpret_cast<uint4*>(&m.obits[lane * 4]) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-  const bool outside = __any_sync(kFull, (ow[0] | ow[1] | ow[2] | ow[3]) != 0u);
+  const uint4 pv = make_uint4(past[0], past[1], past[2], past[3]);
+  *reinterpret_cast<uint4*>(&m.sbits[lane * 4]) = pv;
+  *reinterpret_cast<uint4*>(&m.ebits[lane * 4]) = pv;
+  *reinterpret_cast<uint4*>(&m.obits[lane * 4]) = make_uint4(0u, 0u, 0u, 0u);
+  __syncwarp();
+  const int64_t BL = cu.BL;
+  int64_t t = t0;
+  uint32_t pos = 0;
+  bool outside = false;
+  while (pos < n_valid) {
+    int64_t len = static_cast<int64_t>(n_valid - pos);
+    if (len > BL - t) len = BL - t;
+    mark_segment<IdxT, NIN, T>(m, cu, t, len, pos, lane, outside);
+    pos += static_cast<uint32_t>(len);
+    t = 0;
+  }
   if (lane == 0) {
     m.has_outside = outside ? 1u : 0u;
     m.n_valid = n_valid;
@@ -330,30 +365,42 @@ __device__ __forceinline__ float tile_elem(const uint8_t* buf, const StageMeta<N
   return fill;
 }
 
+// Per-thread constants: the swizzled byte offsets of the 16-byte chunks that
+// hold this thread's 16 elements (identical for every 1024-aligned buffer).
+template <typename T>
+struct ThreadChunks {
+  static constexpr int kVec = 16 / sizeof(T);
+  static constexpr int kChunks = kPerThread / kVec;
+  uint32_t off[kChunks];
+  __device__ __forceinline__ explicit ThreadChunks(uint32_t o) {
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) off[c] = swz<T>(o + c * kVec);
+  }
+};
+
 // This thread's 16 elements [o, o+16) of input k.
 template <typename T, int NIN>
-__device__ __forceinline__ void read_block(const uint8_t* buf, const StageMeta<NIN, T>& m, int k,
-                                           uint32_t o, uint32_t n_tma, uint32_t n_valid,
-                                           float fill, float (&v)[kPerThread]) {
+__device__ __forceinline__ void read_block(const uint8_t* buf, const ThreadChunks<T>& tc,
+                                           const StageMeta<NIN, T>& m, int k, uint32_t o,
+                                           uint32_t n_tma, uint32_t n_valid, float fill,
+                                           float (&v)[kPerThread]) {
   if (o + kPerThread <= n_tma) {
-    constexpr int kVec = 16 / sizeof(T);
 #pragma unroll
-    for (int c = 0; c < kPerThread / kVec; ++c) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(buf + swz<T>(o + c * kVec));
-      unpack16<T>(raw, &v[c * kVec]);
-    }
+    for (int c = 0; c < ThreadChunks<T>::kChunks; ++c)
+      unpack16<T>(*reinterpret_cast<const uint4*>(buf + tc.off[c]), &v[c * ThreadChunks<T>::kVec]);
   } else {
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) v[j] = tile_elem<T, NIN>(buf, m, k, o + j, n_tma, n_valid, fill);
+    for (int j = 0; j < kPerThread; ++j)
+      v[j] = tile_elem<T, NIN>(buf, m, k, o + j, n_tma, n_valid, fill);
   }
 }
 
 template <typename T>
-__device__ __forceinline__ void write_block(uint8_t* buf, uint32_t o, const float (&v)[kPerThread]) {
-  constexpr int kVec = 16 / sizeof(T);
+__device__ __forceinline__ void write_block(uint8_t* buf, const ThreadChunks<T>& tc,
+                                            const float (&v)[kPerThread]) {
 #pragma unroll
-  for (int c = 0; c < kPerThread / kVec; ++c)
-    *reinterpret_cast<uint4*>(buf + swz<T>(o + c * kVec)) = pack16<T>(&v[c * kVec]);
+  for (int c = 0; c < ThreadChunks<T>::kChunks; ++c)
+    *reinterpret_cast<uint4*>(buf + tc.off[c]) = pack16<T>(&v[c * ThreadChunks<T>::kVec]);
 }
 
 // Direct global stores of the elements whose bit is set in `mask`.
@@ -365,110 +412,148 @@ __device__ __forceinline__ void store_direct(T* base, int64_t p, uint32_t mask,
     if ((mask >> j) & 1u) base[p + j] = Cvt<T>::from(v[j]);
 }
 
-// Serial fold of 16 elements in scan order with sequence heads.
+// Bits j of [0, 16) with o + j < limit.
+__device__ __forceinline__ uint32_t below_mask(uint32_t o, uint32_t limit) {
+  if (limit >= o + kPerThread) return 0xffffu;
+  return limit > o ? (1u << (limit - o)) - 1u : 0u;
+}
+
+// Serial fold of 16 elements in scan order with sequence heads.  Leaves the
+// local inclusive prefix of every element in place (a[j] = product of the
+// gates since the last head, b[j] = the state from a zero carry) and returns
+// the thread's aggregate.  Two independent chains (a and b).
 template <bool REV>
-__device__ __forceinline__ Pfx fold16(const float (&a)[kPerThread], const float (&b)[kPerThread],
-                                      uint32_t head) {
+__device__ __forceinline__ Pfx fold16_inplace(float (&a)[kPerThread], float (&b)[kPerThread],
+                                              uint32_t head) {
   constexpr int j0 = REV ? kPerThread - 1 : 0;
-  Pfx p{a[j0], b[j0], kValid | static_cast<int>((head >> j0) & 1u)};
+  float A = a[j0], B = b[j0];
+  int f = kValid | static_cast<int>((head >> j0) & 1u);
   if (head == 0u) {
 #pragma unroll
     for (int jj = 1; jj < kPerThread; ++jj) {
       const int j = REV ? kPerThread - 1 - jj : jj;
-      p.b = fmaf(a[j], p.b, b[j]);
-      p.a *= a[j];
+      B = fmaf(a[j], B, b[j]);
+      A *= a[j];
+      a[j] = A;
+      b[j] = B;
     }
   } else {
 #pragma unroll
     for (int jj = 1; jj < kPerThread; ++jj) {
       const int j = REV ? kPerThread - 1 - jj : jj;
       if ((head >> j) & 1u) {
-        p.a = a[j];
-        p.b = b[j];
-        p.f |= kHead;
+        A = a[j];
+        B = b[j];
+        f |= kHead;
       } else {
-        p.b = fmaf(a[j], p.b, b[j]);
-        p.a *= a[j];
+        B = fmaf(a[j], B, b[j]);
+        A *= a[j];
       }
+      a[j] = A;
+      b[j] = B;
     }
   }
-  return p;
+  return Pfx{A, B, f};
 }
 
-// Tile-level part shared by the forward and backward consumers: combines
-// the per-warp totals, publishes this tile's status and looks back.  Returns
-// the prefix preceding this thread's first element in scan order.
-template <bool REV, typename Sm>
-__device__ __forceinline__ Pfx consumer_tile_prefix(Sm& sm, Pfx thread_excl, Pfx warp_total,
-                                                    bool first_is_head, uint32_t ticket,
-                                                    const TileStatus& st, int warp, int lane) {
-  if (lane == 0) sm.warp_total[warp] = warp_total;
-  consumer_sync();
-  Pfx wex = pfx_empty(), tot = pfx_empty();
-#pragma unroll
-  for (int ww = 0; ww < kConsumerWarps; ++ww) {
-    const int w = REV ? kConsumerWarps - 1 - ww : ww;
-    if (w == warp) wex = tot;
-    tot = compose(tot, sm.warp_total[w]);
+// Elements (bits) that come before the first head in scan order: only these
+// take the carry-in.
+template <bool REV>
+__device__ __forceinline__ uint32_t carry_mask(uint32_t head) {
+  if (head == 0u) return 0xffffu;
+  if (!REV) return (1u << (__ffs(head) - 1)) - 1u;
+  return 0xffffu & ~((2u << (31 - __clz(head))) - 1u);
+}
+
+// Slot hand-off in shared memory: value words, fence, then the tag.
+__device__ __forceinline__ void xs_put(float4* slot, const Pfx& p, uint32_t tag) {
+  volatile float* v = reinterpret_cast<volatile float*>(slot);
+  v[0] = p.a;
+  v[1] = p.b;
+  v[2] = __int_as_float(p.f);
+  __threadfence_block();
+  v[3] = __uint_as_float(tag);
+}
+
+// Bounded wait for a slot tagged `tag`; false on timeout or when another warp
+// of the CTA has given up.
+__device__ __forceinline__ bool xs_get(const float4* slot, uint32_t tag, Pfx& out,
+                                       const volatile int* abort_flag) {
+  const volatile float* v = reinterpret_cast<const volatile float*>(slot);
+  if (__float_as_uint(v[3]) != tag) {
+    const unsigned long long t0 = globaltimer();
+    while (__float_as_uint(v[3]) != tag) {
+      if (*abort_flag || globaltimer() - t0 > kLookbackTimeoutNs) return false;
+    }
   }
-  const bool need_lookback = !first_is_head && ticket > 0;
-  if (warp == 0) {
+  __threadfence_block();
+  out = Pfx{v[0], v[1], __float_as_int(v[2])};
+  return true;
+}
+
+// Prefix of this thread's first element within the whole scan, for one warp
+// of a tile, without any CTA-wide barrier.  Every warp posts its total; the
+// scan-first warp looks back over the preceding tiles and posts the tile's
+// carry-in; each warp composes the totals of the warps before it; the
+// scan-last warp publishes the tile's status.  `ok` turns false when a wait
+// gave up (the caller then leaves its loop after this tile).
+template <bool REV, typename Sm>
+__device__ __forceinline__ Pfx warp_tile_prefix(Sm& sm, uint32_t xi, Pfx thread_excl,
+                                                Pfx warp_total, bool first_is_head,
+                                                uint32_t ticket, const TileStatus& st,
+                                                uint32_t stride, bool te_known, Pfx te_known_val,
+                                                int warp, int lane, bool& ok) {
+  constexpr int kLast = kConsumerWarps - 1;
+  const int lw = REV ? kLast - warp : warp;  // position of this warp in scan order
+  const bool need_lookback = !first_is_head && ticket >= stride;  // else a row's first tile
+  XSlot& slot = sm.xs[xi];
+  if (lane == 0) xs_put(&slot.warp[warp], warp_total, ticket);
+  if (lw == 0 && need_lookback) {
+    Pfx te = te_known_val;
+    if (!te_known) {
+      bool timed_out = false;
+      te = lookback_warp<kLookbackPerLane>(st, ticket, lane, &timed_out, stride);
+      if (timed_out && lane == 0) report(ASCAN_DEV_ERR_LOOKBACK, ticket);
+    }
+    if (lane == 0) xs_put(&slot.te, te, ticket);
+  }
+  // totals of the warps before this one, lane j holding the j-th in scan order
+  Pfx x = pfx_empty();
+  bool got = true;
+  if (lane < lw) got = xs_get(&slot.warp[REV ? kLast - lane : lane], ticket, x, &sm.abort);
+#pragma unroll
+  for (int off = 1; off < kConsumerWarps; off <<= 1) {
+    const Pfx o{__shfl_down_sync(kFull, x.a, off), __shfl_down_sync(kFull, x.b, off),
+                __shfl_down_sync(kFull, x.f, off)};
+    if (lane + off < 32) x = compose(x, o);
+  }
+  const Pfx wex{__shfl_sync(kFull, x.a, 0), __shfl_sync(kFull, x.b, 0), __shfl_sync(kFull, x.f, 0)};
+  const Pfx p_in = compose(wex, thread_excl);
+  Pfx te = pfx_empty();
+  if (lw == kLast) {
+    const Pfx tot = compose(wex, warp_total);
     if (lane == 0) {
       const bool inclusive = (tot.f & kHead) || !need_lookback;
       publish(st, ticket, inclusive ? kStatusInclusive : kStatusAggregate, tot.a, tot.b);
     }
-    if (need_lookback) {
-      Pfx te = pfx_empty();
-      int64_t base = static_cast<int64_t>(ticket) - 1;
-      bool timed_out = false;
-      while (true) {
-        const int64_t q = base - lane;
-        Pfx x = pfx_empty();
-        bool inc = true;
-        if (q >= 0) {
-          const uint32_t s = wait_status(st, static_cast<uint32_t>(q));
-          if (s == kStatusInclusive || s == kStatusAggregate) {
-            const float2 v = ld_relaxed_f2(reinterpret_cast<const float*>(st.vals + q) +
-                                           (s == kStatusInclusive ? 2 : 0));
-            x = Pfx{v.x, v.y, kValid};
-            inc = (s == kStatusInclusive);
-          } else {
-            timed_out = true;
-          }
-        }
-        const unsigned incmask = __ballot_sync(kFull, inc);
-        const int stop = incmask ? (__ffs(incmask) - 1) : 31;
-        if (lane > stop) x = pfx_empty();
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          Pfx o{__shfl_down_sync(kFull, x.a, off), __shfl_down_sync(kFull, x.b, off),
-                __shfl_down_sync(kFull, x.f, off)};
-          if (lane + off < 32) x = compose(o, x);
-        }
-        const Pfx part{__shfl_sync(kFull, x.a, 0), __shfl_sync(kFull, x.b, 0),
-                       __shfl_sync(kFull, x.f, 0)};
-        te = compose(part, te);
-        if (incmask) break;
-        base -= 32;
-      }
-      // A timed-out wait has set the launch's abort word: the producers stop
-      // taking tiles and every consumer leaves through the normal path.
-      if (__any_sync(kFull, timed_out) && lane == 0) report(ASCAN_DEV_ERR_LOOKBACK, ticket);
+    if (need_lookback && !(tot.f & kHead)) {
+      if (lane == 0) got = xs_get(&slot.te, ticket, te, &sm.abort) && got;
+      te = Pfx{__shfl_sync(kFull, te.a, 0), __shfl_sync(kFull, te.b, 0),
+               __shfl_sync(kFull, te.f, 0)};
       if (lane == 0) {
-        if (!(tot.f & kHead)) {
-          const Pfx inc = compose(te, tot);
-          publish(st, ticket, kStatusInclusive, inc.a, inc.b);
-        }
-        sm.te = te;
+        const Pfx inc = compose(te, tot);
+        publish(st, ticket, kStatusInclusive, inc.a, inc.b);
       }
+      ok = __all_sync(kFull, got) && ok;
+      return compose(te, p_in);
     }
   }
-  Pfx te = pfx_empty();
-  if (need_lookback) {
-    consumer_sync();
-    te = sm.te;
+  if (need_lookback && __any_sync(kFull, !(p_in.f & kHead))) {
+    if (lane == 0) got = xs_get(&slot.te, ticket, te, &sm.abort) && got;
+    te = Pfx{__shfl_sync(kFull, te.a, 0), __shfl_sync(kFull, te.b, 0), __shfl_sync(kFull, te.f, 0)};
   }
-  return compose(te, compose(wex, thread_excl));
+  ok = __all_sync(kFull, got) && ok;
+  return compose(te, p_in);
 }
 
 }  // namespace tma

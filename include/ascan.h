@@ -146,7 +146,7 @@ ASCAN_API int ascan_backward(const void* grad, const void* gates, const void* st
  * Arguments, results and other return codes are those of ascan_forward.
  */
 #define ASCAN_NOALLOC_SCRATCH_BYTES (2u << 20)
-#define ASCAN_NOALLOC_MAX_ELEMENTS 429391872ll /* 104832 tiles of 4096 elements */
+#define ASCAN_NOALLOC_MAX_ELEMENTS 536805376ll /* 131056 tiles of 4096 elements */
 ASCAN_API int ascan_forward_noalloc(const void* gates, const void* tokens, void* tokens_out,
                                     void* gates_out, const void* cu_seqlens, int cu_index_type,
                                     int64_t num_seq, int64_t num_channels, int64_t seq_total,
@@ -169,12 +169,17 @@ ASCAN_API int ascan_shift_pad(const void* data, void* out, const void* cu_seqlen
 
 /*
  * Kernel family used by the calls that follow (process-wide):
- *   0  automatic (the default; env ASCAN_IMPL=simple|tma overrides it):
- *      currently the plain kernels, the faster family on B200 so far
+ *   0  automatic (the default; env ASCAN_IMPL=simple|tma|tma-flat|tma-row
+ *      overrides it): the persistent TMA-pipelined kernels whenever
+ *      possible (as 2), the plain kernels otherwise
  *   1  always the plain kernels (128-bit loads, one CTA per tile)
  *   2  the persistent TMA-pipelined kernels whenever every pointer is
  *      16-byte aligned and the array holds at least one 128-byte row,
  *      the plain kernels otherwise
+ *   3  as 2, tiles always dealt in flat order (a tile's predecessor is the
+ *      tile before it in memory)
+ *   4  as 2, tiles dealt tile-major across rows whenever every row is a
+ *      whole number of tiles (a tile's predecessor is in the same row)
  * Both families compute the same results; the switch exists for testing
  * and measurement.  No counterpart in the reference, which has one
  * Triton kernel per case.

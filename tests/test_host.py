@@ -43,9 +43,9 @@ def test_workspace_size_grows_with_problem():
   small = lib.ascan_workspace_size(4, 128, 0)
   big = lib.ascan_workspace_size(1536, 8 * 65536, 0)
   assert small >= 256 and big > small
-  # 4096-element tiles: 4-byte flag + 16-byte value per tile plus a 256-byte header
+  # 4096-element tiles: one 16-byte status slot per tile plus a 256-byte header
   tiles = (1536 * 8 * 65536 + 4095) // 4096
-  assert big >= 256 + 20 * tiles
+  assert big == 256 + 16 * tiles
 
 
 def test_abi_rejects_bad_arguments_without_a_gpu():

@@ -452,3 +452,52 @@ def test_both_kernel_families_agree(dtype, reverse):
     ref = outs["simple"][i].double().cpu().numpy()
     assert_close_to_gold(outs["tma"][i], ref, dtype, f"tma vs simple output {i}",
                          rtol=2 * rtol_of(dtype))
+
+
+# --- tile orders of the persistent kernels ---------------------------------------------
+
+TILE_ORDER_CASES = [
+  # C, cu_seqlens -- every row a whole number of 4096-element tiles, so the
+  # row order applies; 300 rows is the automatic choice on a 148-SM B200
+  (300, [0, 8192]),
+  (300, [0, 4096, 4173, 12288]),
+  (5, [0, 4096 * 6]),                 # row order with fewer rows than CTAs
+  (2, [100, 300, 12288]),             # positions before cu[0] lie in no sequence
+  (7, [0, 1, 4097, 4098, 8192]),
+  (160, [0, 4096 * 4]),
+]
+
+
+@pytest.mark.parametrize("order", ["tma-row", "tma-flat"])
+@pytest.mark.parametrize(("C", "cu_list"), TILE_ORDER_CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_tile_orders_match_oracle(order, C, cu_list, dtype, reverse):
+  from associative_scan_triton import _lib
+  BL = cu_list[-1]
+  S = len(cu_list) - 1
+  g, x = make_inputs(C, BL, dtype=dtype, gate="long", seed=C + BL + S)
+  cu = torch.tensor(cu_list, dtype=torch.int64, device=DEV)
+  mask = in_sequence_mask(C, BL, cu)
+  dy = torch.randn(C, BL, generator=torch.Generator().manual_seed(5)).to(DEV, dtype)
+  try:
+    _lib.set_implementation(order)
+    y = torch.full_like(x, 7.0)
+    gp = g.clone()
+    ast.forward_scan_full(gp, x, cu, (S, 1, C), REVERSE=reverse, CHUNK_SIZE=2, TESTING=True,
+                          tokens_out=y)
+    dx, dg = torch.full_like(x, 7.0), torch.full_like(x, 7.0)
+    ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, (S, 1, C), CHUNK_SIZE=2,
+                                 CAUSAL=not reverse)
+    torch.cuda.synchronize()
+  finally:
+    _lib.set_implementation("auto")
+  _lib.check_device_error()
+  gold_y, gold_a = oracle.scan_fwd(g, x, cu, reverse=reverse)
+  assert_close_to_gold(y, gold_y, dtype, f"{order} y", mask=mask)
+  assert_close_to_gold(gp, gold_a, dtype, f"{order} gate products", mask=mask)
+  gdx, gdg = oracle.scan_bwd(dy, g, y, cu, causal=not reverse)
+  assert_close_to_gold(dx, gdx, dtype, f"{order} dx", mask=mask)
+  assert_close_to_gold(dg, gdg, dtype, f"{order} dg", mask=mask)
+  # positions outside every sequence are never written
+  assert (y[:, ~mask[0]] == 7.0).all() and (dx[:, ~mask[0]] == 7.0).all()

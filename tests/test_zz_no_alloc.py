@@ -25,7 +25,7 @@ from associative_scan_triton import _lib
 from scan_testlib import assert_close_to_gold, cu_of, make_inputs
 
 ASCAN_ETOOLARGE = -5
-MAX_ELEMENTS = 429391872
+MAX_ELEMENTS = 536805376
 
 
 def _noalloc():
@@ -82,4 +82,4 @@ def test_forward_noalloc_rejects_sizes_beyond_its_scratch():
           MAX_ELEMENTS + 1, 1, 0, 0, torch.cuda.current_stream().cuda_stream)
   assert rc == ASCAN_ETOOLARGE
   assert "fixed scratch" in _lib.strerror(rc)
-  assert np.int64(MAX_ELEMENTS) // 4096 == 104832  # whole 4096-element tiles
+  assert np.int64(MAX_ELEMENTS) // 4096 == 131056  # whole 4096-element tiles
