@@ -44,7 +44,7 @@ FWD_BYTES_PER_ELEM = 3 * 4    # read g, x; write y (fp32)
 BWD_BYTES_PER_ELEM = 5 * 4    # read dy, g, h; write dx, dg
 STEP_BYTES_PER_ELEM = FWD_BYTES_PER_ELEM + BWD_BYTES_PER_ELEM
 L2_BYTES = 126 * 2**20
-PROFILE_SUMMARY = REPO / "profiles" / "scan_bwd_kernel_config2.md"
+PROFILE_SUMMARY = REPO / "profiles" / "scan_bwd_tma_kernel_B8_T4096_C1536_f32.md"
 
 
 def _peaks() -> tuple[float, str]:
@@ -59,7 +59,7 @@ def _profile_traffic() -> float | None:
   """DRAM bytes per bwd launch from the committed ncu summary, if present."""
   try:
     for line in PROFILE_SUMMARY.read_text().splitlines():
-      if line.startswith("traffic_bytes_per_launch_config2:"):
+      if line.startswith("traffic_bytes_per_launch:"):
         return float(line.split(":", 1)[1].strip())
   except OSError:
     pass
@@ -373,7 +373,7 @@ def run_ours(args) -> dict | None:
     "fwd_gbs": round(fwd_achieved, 1),
     "bwd_ms": round(bwd_ms, 5),
     "roofline": {
-      "bound": "hbm", "kernel": "scan_bwd_kernel (fused backward)",
+      "bound": "hbm", "kernel": "scan_bwd_tma_kernel (fused backward, persistent TMA)",
       "achieved": round(bwd_achieved, 1), "peak": peak, "unit": "GB/s",
       "frac": round(bwd_achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
       "traffic": traffic,
