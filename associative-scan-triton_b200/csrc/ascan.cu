@@ -444,10 +444,19 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
     t_flat = (static_cast<int64_t>(tile0) * kTileElems) % BL;
   }
   uint32_t abort_seen = 0u;
+  uint32_t iter = 0u;
   while (true) {
     if (ticket >= num_tiles || abort_seen) ticket = kDone;
-    const uint32_t abort_next = (lane == 0 && ticket != kDone) ? ld_volatile_u32(st.abort) : 0u;
-    if (!mbar_wait(&sm.empty[stage], phase ^ 1u)) {
+    // Stop early when the launch was aborted: the CTA's own word every tile
+    // (shared memory), the launch-wide word every 16th tile -- a global load
+    // on every tile would put an L2 round trip on the producer's path.
+    uint32_t abort_next = 0u;
+    if (lane == 0 && ticket != kDone) {
+      abort_next = static_cast<uint32_t>(*reinterpret_cast<volatile int*>(&sm.abort));
+      if ((iter & 15u) == 15u) abort_next |= ld_volatile_u32(st.abort);
+    }
+    ++iter;
+    if (!mbar_wait_warp(&sm.empty[stage], phase ^ 1u)) {
       if (lane == 0) {
         report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffeull);
         set_aborted(st);
@@ -515,7 +524,7 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
   // barrier is still in the phase that load armed).
 #pragma unroll
   for (int s = 0; s < NS; ++s)
-    if (pending[s]) mbar_wait(&sm.full[s], last_parity[s]);
+    if (pending[s]) mbar_wait_warp(&sm.full[s], last_parity[s]);  // pending is warp-uniform
 }
 
 template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS>
@@ -572,9 +581,12 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
   constexpr int kPartBytes = Fmt<T>::kBytes / kConsumerWarps;
   uint32_t stage = 0, phase = 0, obuf = 0, xi = 0;
   bool ok = true;
-  while (ok) {
-    const bool got = __all_sync(kFull, mbar_wait(&sm.full[stage], phase));
-    if (!got || *reinterpret_cast<volatile int*>(&sm.abort)) {
+  while (true) {
+    // Every exit is decided by one warp-wide vote: this warp's own status,
+    // the stage's arrival and the CTA's abort word.
+    bool go = ok && mbar_wait_warp(&sm.full[stage], phase);  // ok is warp-uniform
+    go = __all_sync(kFull, go && *reinterpret_cast<volatile int*>(&sm.abort) == 0);
+    if (!go) {
       ok = false;
       break;
     }
@@ -744,9 +756,12 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
   constexpr int kPartBytes = Fmt<T>::kBytes / kConsumerWarps;
   uint32_t stage = 0, phase = 0, obuf = 0, xi = 0;
   bool ok = true;
-  while (ok) {
-    const bool got = __all_sync(kFull, mbar_wait(&sm.full[stage], phase));
-    if (!got || *reinterpret_cast<volatile int*>(&sm.abort)) {
+  while (true) {
+    // Every exit is decided by one warp-wide vote: this warp's own status,
+    // the stage's arrival and the CTA's abort word.
+    bool go = ok && mbar_wait_warp(&sm.full[stage], phase);  // ok is warp-uniform
+    go = __all_sync(kFull, go && *reinterpret_cast<volatile int*>(&sm.abort) == 0);
+    if (!go) {
       ok = false;
       break;
     }

@@ -365,6 +365,13 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   return t;
 }
 
+// True once more than kLookbackTimeoutNs have passed since t0.  The
+// difference is taken signed, so a timer reading that steps back never
+// counts as an expired wait.
+__device__ __forceinline__ bool wait_expired(unsigned long long t0) {
+  return static_cast<long long>(globaltimer() - t0) > static_cast<long long>(kLookbackTimeoutNs);
+}
+
 // Tile status records, one 16-byte slot per ticket: two 64-bit words
 // {a, state} and {b, state} written by one relaxed vector store.  Each
 // aligned 64-bit word is single-copy atomic, states only grow
@@ -425,7 +432,7 @@ __device__ __forceinline__ uint32_t wait_status(const TileStatus& st, uint32_t t
     s = read_status(st, ticket, a, b);
     if (s != kStatusNone) return s;
     if (launch_aborted(st)) return kStatusNone;
-    if (globaltimer() - t0 > kLookbackTimeoutNs) {
+    if (wait_expired(t0)) {
       set_aborted(st);
       return kStatusNone;
     }
@@ -485,7 +492,7 @@ __device__ __forceinline__ Pfx lookback_warp(const TileStatus& st, uint32_t tick
       if (poll == 0) t0 = globaltimer();
       __nanosleep(ns);
       if (ns < 256) ns <<= 1;
-      const bool give_up = launch_aborted(st) || (globaltimer() - t0 > kLookbackTimeoutNs);
+      const bool give_up = launch_aborted(st) || wait_expired(t0);
       if (__any_sync(kFull, give_up)) {
         if (lane == 0) set_aborted(st);
         lost = true;  // unpublished slots count as empty records

@@ -94,14 +94,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase of `parity` to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Bounded wait of a whole warp for the phase of `parity` to complete: every
+// lane polls (so every lane acquires), and both the completion and the
+// timeout are decided by warp votes, so all 32 lanes leave together with the
+// same result.  All lanes must call it.  false on timeout.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+  bool done = mbar_try_wait(bar, parity);
+  if (__all_sync(kFull, done)) return true;
   const unsigned long long t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kLookbackTimeoutNs) return false;
+  while (true) {
+    if (!done) done = mbar_try_wait(bar, parity);
+    if (__all_sync(kFull, done)) return true;
+    if (__any_sync(kFull, wait_expired(t0))) return false;
   }
-  return true;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
@@ -475,19 +480,25 @@ __device__ __forceinline__ void xs_put(float4* slot, const Pfx& p, uint32_t tag)
   v[3] = __uint_as_float(tag);
 }
 
-// Bounded wait for a slot tagged `tag`; false on timeout or when another warp
-// of the CTA has given up.
-__device__ __forceinline__ bool xs_get(const float4* slot, uint32_t tag, Pfx& out,
-                                       const volatile int* abort_flag) {
+// Bounded wait of a whole warp for slot hand-offs: each lane with `need`
+// waits for its `slot` to carry `tag` and then reads it into `out` (other
+// lanes leave `out` alone).  Completion, timeout and the CTA's abort word are
+// decided by warp votes, so the result is the same in all lanes and the warp
+// never splits.  All lanes must call it.  false on timeout or abort.
+__device__ __forceinline__ bool xs_get_warp(const float4* slot, bool need, uint32_t tag,
+                                            Pfx& out, const volatile int* abort_flag) {
   const volatile float* v = reinterpret_cast<const volatile float*>(slot);
-  if (__float_as_uint(v[3]) != tag) {
+  bool have = !need || __float_as_uint(v[3]) == tag;
+  if (!__all_sync(kFull, have)) {
     const unsigned long long t0 = globaltimer();
-    while (__float_as_uint(v[3]) != tag) {
-      if (*abort_flag || globaltimer() - t0 > kLookbackTimeoutNs) return false;
+    while (true) {
+      if (!have) have = __float_as_uint(v[3]) == tag;
+      if (__all_sync(kFull, have)) break;
+      if (__any_sync(kFull, *abort_flag != 0 || wait_expired(t0))) return false;
     }
   }
   __threadfence_block();
-  out = Pfx{v[0], v[1], __float_as_int(v[2])};
+  if (need) out = Pfx{v[0], v[1], __float_as_int(v[2])};
   return true;
 }
 
@@ -519,8 +530,9 @@ __device__ __forceinline__ Pfx warp_tile_prefix(Sm& sm, uint32_t xi, Pfx thread_
   }
   // totals of the warps before this one, lane j holding the j-th in scan order
   Pfx x = pfx_empty();
-  bool got = true;
-  if (lane < lw) got = xs_get(&slot.warp[REV ? kLast - lane : lane], ticket, x, &sm.abort);
+  const bool before = lane < lw;
+  bool got = xs_get_warp(&slot.warp[before ? (REV ? kLast - lane : lane) : 0], before, ticket, x,
+                         &sm.abort);
 #pragma unroll
   for (int off = 1; off < kConsumerWarps; off <<= 1) {
     const Pfx o{__shfl_down_sync(kFull, x.a, off), __shfl_down_sync(kFull, x.b, off),
@@ -537,22 +549,18 @@ __device__ __forceinline__ Pfx warp_tile_prefix(Sm& sm, uint32_t xi, Pfx thread_
       publish(st, ticket, inclusive ? kStatusInclusive : kStatusAggregate, tot.a, tot.b);
     }
     if (need_lookback && !(tot.f & kHead)) {
-      if (lane == 0) got = xs_get(&slot.te, ticket, te, &sm.abort) && got;
-      te = Pfx{__shfl_sync(kFull, te.a, 0), __shfl_sync(kFull, te.b, 0),
-               __shfl_sync(kFull, te.f, 0)};
+      got = xs_get_warp(&slot.te, true, ticket, te, &sm.abort) && got;
       if (lane == 0) {
         const Pfx inc = compose(te, tot);
         publish(st, ticket, kStatusInclusive, inc.a, inc.b);
       }
-      ok = __all_sync(kFull, got) && ok;
+      ok = got && ok;  // got is warp-uniform
       return compose(te, p_in);
     }
   }
-  if (need_lookback && __any_sync(kFull, !(p_in.f & kHead))) {
-    if (lane == 0) got = xs_get(&slot.te, ticket, te, &sm.abort) && got;
-    te = Pfx{__shfl_sync(kFull, te.a, 0), __shfl_sync(kFull, te.b, 0), __shfl_sync(kFull, te.f, 0)};
-  }
-  ok = __all_sync(kFull, got) && ok;
+  if (need_lookback && __any_sync(kFull, !(p_in.f & kHead)))
+    got = xs_get_warp(&slot.te, true, ticket, te, &sm.abort) && got;
+  ok = got && ok;  // got is warp-uniform
   return compose(te, p_in);
 }
 
