@@ -248,16 +248,26 @@ struct CuView {
     if (s) return s[i];
     return cu_at(g, i, BL);
   }
-  // first i in [lo, hi) with at(i) >= v (hi if none); entries assumed sorted
-  __device__ __forceinline__ int64_t lower_bound(int64_t lo, int64_t hi, int64_t v) const {
-    while (lo < hi) {
-      const int64_t m = (lo + hi) >> 1;
-      if (at(m) < v)
-        lo = m + 1;
-      else
-        hi = m;
+  // First i in [lo, hi) with at(i) >= v (hi if none), for sorted entries;
+  // any input gives an index in [lo, hi].  Warp-wide: all lanes call and get
+  // the same result.  Each round probes 32 evenly spaced entries at once, so
+  // up to 32 entries take one round of loads and a ballot.
+  __device__ __forceinline__ int64_t lower_bound_warp(int64_t lo, int64_t hi, int64_t v,
+                                                      int lane) const {
+    while (hi - lo > 32) {
+      const int64_t step = (hi - lo + 31) / 32;
+      const int64_t idx = lo + lane * step;
+      const unsigned ge = __ballot_sync(kFull, idx < hi && at(idx) >= v);
+      if (ge & 1u) return lo;
+      const int f = ge ? __ffs(ge) - 1 : 32;          // first probe at or above v
+      const int64_t below = lo + static_cast<int64_t>(f - 1) * step;  // last probe below v
+      const int64_t next_hi = f < 32 ? lo + static_cast<int64_t>(f) * step : hi;
+      lo = below + 1;
+      hi = next_hi < hi ? next_hi : hi;
     }
-    return lo;
+    const int64_t idx = lo + lane;
+    const unsigned ge = __ballot_sync(kFull, idx < hi && at(idx) >= v);
+    return ge ? lo + (__ffs(ge) - 1) : hi;
   }
 };
 
@@ -267,8 +277,10 @@ __device__ __forceinline__ void or_bit(uint32_t* words, uint32_t e) {
 
 // Marks, for row positions [t, t+len) sitting at tile offset `pos`, the
 // sequence starts (cu[i], i < S), the sequence ends (cu[j]-1, j >= 1) and the
-// positions before cu[0] (which belong to no sequence).  One binary search
-// per segment; the heads found are spread over the 32 lanes.
+// positions before cu[0] (which belong to no sequence).  One warp-wide search
+// for the first boundary at or after t, then one pass over the boundaries in
+// [t, t+len]: boundary v = cu[i] starts a sequence at v and ends one at v-1.
+// Called by all lanes.
 template <typename IdxT, int NIN, typename T>
 __device__ __forceinline__ void mark_segment(StageMeta<NIN, T>& m, const CuView<IdxT>& cu,
                                              int64_t t, int64_t len, uint32_t pos, int lane,
@@ -285,29 +297,19 @@ __device__ __forceinline__ void mark_segment(StageMeta<NIN, T>& m, const CuView<
     }
     outside = true;
   }
-  const int64_t i0 = cu.lower_bound(0, cu.S, t);
-  // starts cu[i] in [t, end) and ends cu[j]-1 in [t, end), both from i0 on
+  const int64_t i0 = cu.lower_bound_warp(0, cu.S + 1, t, lane);
   for (int64_t i = i0 + lane;; i += 32) {
-    bool any = false;
-    if (i < cu.S) {
+    bool in = false;  // this lane's boundary lies in [t, end]
+    if (i <= cu.S) {
       const int64_t v = cu.at(i);
-      if (v < end) {
-        any = true;
-        if (v >= t) or_bit(m.sbits, pos + static_cast<uint32_t>(v - t));
+      if (v <= end) {
+        in = true;
+        if (i < cu.S && v >= t && v < end) or_bit(m.sbits, pos + static_cast<uint32_t>(v - t));
+        if (i >= 1 && v > t) or_bit(m.ebits, pos + static_cast<uint32_t>(v - 1 - t));
       }
     }
-    if (!__any_sync(kFull, any)) break;
-  }
-  for (int64_t j = (i0 > 0 ? i0 : 1) + lane;; j += 32) {
-    bool any = false;
-    if (j <= cu.S) {
-      const int64_t v = cu.at(j) - 1;
-      if (v < end) {
-        any = true;
-        if (v >= t) or_bit(m.ebits, pos + static_cast<uint32_t>(v - t));
-      }
-    }
-    if (!__any_sync(kFull, any)) break;
+    // sorted boundaries: another round only if the last lane's was still inside
+    if (!__shfl_sync(kFull, in, 31)) break;
   }
 }
 
