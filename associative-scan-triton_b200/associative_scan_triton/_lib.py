@@ -1,8 +1,9 @@
 """ctypes binding of the native library ``libascan_b200.so`` (C ABI: include/ascan.h).
 
-Every op of this package reaches the GPU through the three entry points bound
-here -- ``ascan_forward``, ``ascan_backward`` and ``ascan_shift_pad`` -- with
-raw device pointers, sizes and torch's current CUDA stream.  There is no CPU
+Every op of this package reaches the GPU through the entry points bound here --
+``ascan_forward``, ``ascan_backward``, ``ascan_shift_pad`` and, for time
+slabs, ``ascan_forward_slab`` / ``ascan_backward_slab`` -- with raw device
+pointers, sizes and torch's current CUDA stream.  There is no CPU
 path: a missing library, a CPU tensor or a machine without CUDA raises.
 
 Device-side checks (malformed ``cu_seqlens``, a look-back that gave up) set a
@@ -41,6 +42,8 @@ EXPORTED_SYMBOLS = (
   "ascan_forward",
   "ascan_forward_noalloc",
   "ascan_backward",
+  "ascan_forward_slab",
+  "ascan_backward_slab",
   "ascan_shift_pad",
   "ascan_set_implementation",
   "ascan_get_implementation",
@@ -74,6 +77,11 @@ def _bind(lib) -> None:
   lib.ascan_forward.argtypes = [p, p, p, p, p, ci, i64, i64, i64, ci, ci, p, sz, p]
   lib.ascan_backward.restype = ci
   lib.ascan_backward.argtypes = [p, p, p, p, p, p, ci, i64, i64, i64, ci, ci, p, sz, p]
+  lib.ascan_forward_slab.restype = ci
+  lib.ascan_forward_slab.argtypes = [p, p, p, p, p, ci, i64, i64, i64, ci, ci, p, p, p, sz, p]
+  lib.ascan_backward_slab.restype = ci
+  lib.ascan_backward_slab.argtypes = [p, p, p, p, p, p, ci, i64, i64, i64, ci, ci, p, p, p, p,
+                                      sz, p]
   lib.ascan_shift_pad.restype = ci
   lib.ascan_shift_pad.argtypes = [p, p, p, ci, i64, i64, i64, ci, ctypes.c_double, ci, ci, p]
   lib.ascan_set_implementation.restype = ci
@@ -308,6 +316,84 @@ def backward(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
       d_gates.data_ptr(), cu_seqlens.data_ptr(), INDEX_CODES[cu_seqlens.dtype], int(num_seq),
       C, BL, dcode, int(bool(causal)), ws.data_ptr(), ws.numel(), _stream_ptr(device))
   _finish(rc, "ascan_backward", device)
+
+
+def _row_array(name: str, t: torch.Tensor | None, C: int, width: int, device) -> int | None:
+  """Pointer of a per-row float32 array [C] (width 1) or [C, 2] (width 2)."""
+  if t is None:
+    return None
+  _require_cuda(name, t, device)
+  if t.dtype != torch.float32 or not t.is_contiguous() or t.numel() != C * width:
+    raise ValueError(f"{name} must be a contiguous float32 tensor of {C * width} elements")
+  return t.data_ptr()
+
+
+def forward_slab(gates: torch.Tensor, tokens: torch.Tensor, tokens_out: torch.Tensor | None,
+                 gates_out: torch.Tensor | None, cu_seqlens: torch.Tensor, num_seq: int,
+                 num_channels: int, reverse: bool, row_carry: torch.Tensor | None = None,
+                 row_aggregate: torch.Tensor | None = None) -> None:
+  """ascan_forward_slab: the forward over one time slab of every row, with an
+  optional carried (gate product, state) per row and an optional per-row
+  aggregate output; ``tokens_out=None`` makes it an aggregate-only pass."""
+  tensors = [("gates", gates), ("tokens", tokens)]
+  if tokens_out is not None:
+    tensors.append(("tokens_out", tokens_out))
+  if gates_out is not None:
+    tensors.append(("gates_out", gates_out))
+  device = _check_inputs(tensors, cu_seqlens, num_seq)
+  C, BL = _layout(tokens, num_channels)
+  for name, t in tensors:
+    if _layout(t, num_channels) != (C, BL):
+      raise ValueError(f"{name} shape {tuple(t.shape)} does not match tokens {tuple(tokens.shape)}")
+  carry = _row_array("row_carry", row_carry, C, 2, device)
+  agg = _row_array("row_aggregate", row_aggregate, C, 2, device)
+  lib = load()
+  dcode = DTYPE_CODES[tokens.dtype]
+  with torch.cuda.device(device):
+    ws = _workspace(C, BL, dcode, device)
+    rc = lib.ascan_forward_slab(
+      gates.data_ptr(), tokens.data_ptr(),
+      tokens_out.data_ptr() if tokens_out is not None else None,
+      gates_out.data_ptr() if gates_out is not None else None,
+      cu_seqlens.data_ptr(), INDEX_CODES[cu_seqlens.dtype], int(num_seq), C, BL, dcode,
+      int(bool(reverse)), carry, agg, ws.data_ptr(), ws.numel(), _stream_ptr(device))
+  _finish(rc, "ascan_forward_slab", device)
+
+
+def backward_slab(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
+                  d_tokens: torch.Tensor | None, d_gates: torch.Tensor | None,
+                  cu_seqlens: torch.Tensor, num_seq: int, num_channels: int, causal: bool,
+                  row_carry: torch.Tensor | None = None,
+                  row_state_halo: torch.Tensor | None = None,
+                  row_aggregate: torch.Tensor | None = None) -> None:
+  """ascan_backward_slab: the fused backward over one time slab of every row,
+  with an optional additive adjoint term per row, the state neighbour from
+  the adjacent slab and an optional per-row aggregate output; ``d_tokens`` and
+  ``d_gates`` both None make it an aggregate-only pass."""
+  tensors = [("grad", grad), ("gates", gates), ("states", states)]
+  if (d_tokens is None) != (d_gates is None):
+    raise ValueError("d_tokens and d_gates are given together or not at all")
+  if d_tokens is not None:
+    tensors += [("d_tokens", d_tokens), ("d_gates", d_gates)]
+  device = _check_inputs(tensors, cu_seqlens, num_seq)
+  C, BL = _layout(grad, num_channels)
+  for name, t in tensors:
+    if _layout(t, num_channels) != (C, BL):
+      raise ValueError(f"{name} shape {tuple(t.shape)} does not match grad {tuple(grad.shape)}")
+  carry = _row_array("row_carry", row_carry, C, 1, device)
+  halo = _row_array("row_state_halo", row_state_halo, C, 1, device)
+  agg = _row_array("row_aggregate", row_aggregate, C, 2, device)
+  lib = load()
+  dcode = DTYPE_CODES[grad.dtype]
+  with torch.cuda.device(device):
+    ws = _workspace(C, BL, dcode, device)
+    rc = lib.ascan_backward_slab(
+      grad.data_ptr(), gates.data_ptr(), states.data_ptr(),
+      d_tokens.data_ptr() if d_tokens is not None else None,
+      d_gates.data_ptr() if d_gates is not None else None,
+      cu_seqlens.data_ptr(), INDEX_CODES[cu_seqlens.dtype], int(num_seq), C, BL, dcode,
+      int(bool(causal)), carry, halo, agg, ws.data_ptr(), ws.numel(), _stream_ptr(device))
+  _finish(rc, "ascan_backward_slab", device)
 
 
 def shift_pad(data: torch.Tensor, out: torch.Tensor, cu_seqlens: torch.Tensor,

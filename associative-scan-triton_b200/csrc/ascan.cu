@@ -114,17 +114,35 @@ __device__ __forceinline__ Pfx tile_prefix(Pfx warp_total, bool first_is_head, u
   return compose(te, wex);
 }
 
+// Per-row inputs and outputs of a time slab: the launch covers columns
+// [t0, t1) of every row of a longer sequence axis, and the rest of each row
+// lives elsewhere (another GPU).  All pointers are nullable; only the
+// persistent TMA kernels take them.
+//   carry: forward: [C][2] = (gate product, state) carried into each row's
+//          first element in scan order; backward: [C] = additive term for the
+//          adjoint at that element (its successor gate times successor adjoint)
+//   halo:  backward: [C] = state neighbour of the row element whose neighbour
+//          lies outside the slab (h[t0-1] causal, h[t1] anti-causal)
+//   agg:   [C][2] = inclusive (gate product, value) at each row's last element
+//          in scan order
+struct RowIO {
+  const float* carry;
+  const float* halo;
+  float* agg;
+};
+
 template <typename T, typename IdxT>
 struct FwdArgs {
   const T* g;
   const T* x;
-  T* y;
+  T* y;     // nullable with RowIO.agg: aggregate-only pass
   T* gout;
   const IdxT* cu;
   int64_t S, BL, N;
   uint32_t num_tiles;
   uint32_t* ticket;
   TileStatus st;
+  RowIO io;
 };
 
 // Row position of flat index p.
@@ -219,13 +237,14 @@ struct BwdArgs {
   const T* dy;
   const T* g;
   const T* h;
-  T* dx;
+  T* dx;    // nullable together with dg: aggregate-only pass
   T* dg;
   const IdxT* cu;
   int64_t S, BL, N;
   uint32_t num_tiles;
   uint32_t* ticket;
   TileStatus st;
+  RowIO io;
 };
 
 // Element physically after this lane's vector in row r (lane+1, or lane 0 of
@@ -527,7 +546,9 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
     if (pending[s]) mbar_wait_warp(&sm.full[s], last_parity[s]);  // pending is warp-uniform
 }
 
-template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS>
+// IO: the launch serves a time slab (RowIO in use or no outputs); compiled
+// separately so the ordinary kernels carry none of that code.
+template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO>
 __global__ void __launch_bounds__(tma::kThreads, 1)
     scan_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_g,
                         const __grid_constant__ CUtensorMap map_x,
@@ -606,12 +627,18 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
         REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
     const bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
     const Pfx te_meta{__uint_as_float(m.te_raw[0]), __uint_as_float(m.te_raw[2]), kValid};
+    // time slabs: row ends in scan order, where the row aggregate is taken
+    const uint32_t lastmask =
+        IO && args.io.agg ? ((REV ? m.sbits[bit_word] : m.ebits[bit_word]) >> bit_shift) & 0xffffu
+                          : 0u;
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[stage]);
     if (++stage == NS) {
       stage = 0;
       phase ^= 1u;
     }
+    if (IO && args.io.carry != nullptr && head != 0u)
+      apply_row_carry<REV>(a, b, head, p0 + o, BL, args.io.carry);
 
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(a, b, head), lane, ex, wtot);
@@ -619,6 +646,7 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
                                         sch.stride, te_known, te_meta, warp, lane, ok);
     // a, b hold the local prefixes: h = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV>(head);
+    if (IO && lastmask != 0u) record_row_agg<REV>(a, b, lastmask, cm, P, p0 + o, BL, args.io.agg);
     if (cm == 0xffffu) {
 #pragma unroll
       for (int j = 0; j < kPerThread; ++j) {
@@ -634,13 +662,15 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
         }
       }
     }
+    const bool store = !IO || args.y != nullptr;  // false: aggregate-only pass
     const uint32_t valid = below_mask(o, n_valid) & ~omask;
-    uint32_t direct = valid;
+    uint32_t direct = store ? valid : 0u;
     if (lane == 0) bulk_wait_read<1>();  // this warp's slice of staging buffer obuf is free
     __syncwarp();
     // this warp's slice goes out by TMA when it lies wholly inside the tile's
     // TMA-covered part (never past a row end or the array end)
-    const bool slice_tma = !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
+    const bool slice_tma =
+        store && !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
     if (slice_tma) {
       write_block<T>(sm.out[obuf][0], tc, b);
       if constexpr (GATES_OUT) write_block<T>(sm.out[obuf][1], tc, a);
@@ -671,7 +701,7 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
   if (lane == 0) bulk_wait_all();
 }
 
-template <typename T, typename IdxT, bool CAUSAL, int NS>
+template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO>
 __global__ void __launch_bounds__(tma::kThreads, 1)
     scan_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dy,
                         const __grid_constant__ CUtensorMap map_g,
@@ -826,26 +856,36 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
       hv[kPerThread - 1] = h_nb;
     }
     const uint32_t head = CAUSAL ? emask : smask;
-    const uint32_t tail = CAUSAL ? smask : emask;
+    uint32_t tail = CAUSAL ? smask : emask;
+    // time slabs: carried adjoint at the row's first element in scan order,
+    // state neighbour from outside the slab, aggregate at the row's last element
+    const uint32_t lastmask = IO && args.io.agg ? tail : 0u;
+    if (IO && args.io.carry != nullptr && head != 0u)
+      apply_row_carry_adjoint<CAUSAL>(gv, dyv, head, p0 + o, BL, args.io.carry);
+    if (IO && args.io.halo != nullptr && tail != 0u)
+      tail &= ~apply_row_halo<CAUSAL>(hv, tail, p0 + o, BL, args.io.halo);
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(gv, dyv, head), lane, ex, wtot);
     const Pfx P = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
                                         sch.stride, te_known, te_meta, warp, lane, ok);
     // gv, dyv hold the local prefixes: dh = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV>(head);
+    if (IO && lastmask != 0u) record_row_agg<REV>(gv, dyv, lastmask, cm, P, p0 + o, BL, args.io.agg);
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
       const float d = ((cm >> j) & 1u) ? fmaf(gv[j], P.b, dyv[j]) : dyv[j];
       dyv[j] = d;                                    // dx
       gv[j] = ((tail >> j) & 1u) ? 0.f : d * hv[j];  // dg
     }
+    const bool store = !IO || args.dx != nullptr;  // false: aggregate-only pass
     const uint32_t valid = below_mask(o, n_valid) & ~omask;
-    uint32_t direct = valid;
+    uint32_t direct = store ? valid : 0u;
     if (lane == 0) bulk_wait_read<1>();  // this warp's slice of staging buffer obuf is free
     __syncwarp();
     // this warp's slice goes out by TMA when it lies wholly inside the tile's
     // TMA-covered part (never past a row end or the array end)
-    const bool slice_tma = !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
+    const bool slice_tma =
+        store && !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
     if (slice_tma) {
       write_block<T>(sm.out[obuf][0], tc, dyv);
       write_block<T>(sm.out[obuf][1], tc, gv);
@@ -1096,15 +1136,18 @@ static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, cudaStream_t s) {
   const int64_t rows = a.N / tma::Fmt<T>::kElemsPerRow;
   CUtensorMap mg, mx, my, mgo;
   constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;  // stores: one warp's slice
+  // an aggregate-only pass stores nothing: its output map is a never-used view of g
   if (!make_map<T>(&mg, a.g, rows) || !make_map<T>(&mx, a.x, rows) ||
-      !make_map<T>(&my, a.y, rows, kPart))
+      !make_map<T>(&my, a.y ? a.y : a.g, rows, kPart))
     return 0;
   if (GOUT) {
     if (!make_map<T>(&mgo, a.gout, rows, kPart)) return 0;
   } else {
     mgo = my;
   }
-  auto kern = scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS>;
+  const bool io = a.io.carry || a.io.halo || a.io.agg || !a.y;
+  auto kern = io ? scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, true>
+                 : scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false>;
   int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
   tma::TileSched sch = make_sched(a.num_tiles, a.N, a.BL, a.S);
   void* params[] = {&mg, &mx, &my, &mgo, const_cast<FwdArgs<T, IdxT>*>(&a), &n_tma_total, &sch};
@@ -1120,10 +1163,12 @@ static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, cudaStream_t s) {
   CUtensorMap mdy, mg, mh, mdx, mdg;
   constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;  // stores: one warp's slice
   if (!make_map<T>(&mdy, a.dy, rows) || !make_map<T>(&mg, a.g, rows) ||
-      !make_map<T>(&mh, a.h, rows) || !make_map<T>(&mdx, a.dx, rows, kPart) ||
-      !make_map<T>(&mdg, a.dg, rows, kPart))
+      !make_map<T>(&mh, a.h, rows) || !make_map<T>(&mdx, a.dx ? a.dx : a.dy, rows, kPart) ||
+      !make_map<T>(&mdg, a.dg ? a.dg : a.dy, rows, kPart))
     return 0;
-  auto kern = scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS>;
+  const bool io = a.io.carry || a.io.halo || a.io.agg || !a.dx;
+  auto kern = io ? scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, true>
+                 : scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false>;
   int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
   tma::TileSched sch = make_sched(a.num_tiles, a.N, a.BL, a.S);
   void* params[] = {&mdy, &mg, &mh, &mdx, &mdg, const_cast<BwdArgs<T, IdxT>*>(&a), &n_tma_total,
@@ -1150,7 +1195,7 @@ static void fwd_dispatch(const FwdArgs<T, IdxT>& a, bool reverse, bool gout, cud
 template <typename T, typename IdxT>
 static int fwd_typed(const void* g, const void* x, void* y, void* gout, const void* cu,
                      int64_t S, int64_t C, int64_t BL, int reverse, const Workspace& w,
-                     cudaStream_t s) {
+                     cudaStream_t s, const RowIO& io = RowIO{nullptr, nullptr, nullptr}) {
   FwdArgs<T, IdxT> a;
   a.g = static_cast<const T*>(g);
   a.x = static_cast<const T*>(x);
@@ -1163,8 +1208,20 @@ static int fwd_typed(const void* g, const void* x, void* y, void* gout, const vo
   a.num_tiles = static_cast<uint32_t>(tiles_of(a.N));
   a.ticket = w.ticket;
   a.st = w.st;
+  a.io = io;
   const bool vec = aligned16(g) && aligned16(x) && aligned16(y) && (!gout || aligned16(gout));
   constexpr int kVec = 16 / sizeof(T);
+  // row I/O and absent outputs exist only in the persistent TMA kernels
+  const bool slab = io.carry || io.halo || io.agg || !y;
+  if (slab) {
+    if (!vec || a.N < tma::Fmt<T>::kElemsPerRow) return ASCAN_EINVAL;
+    int rc;
+    if (reverse)
+      rc = gout ? launch_fwd_tma<T, IdxT, true, true>(a, s) : launch_fwd_tma<T, IdxT, true, false>(a, s);
+    else
+      rc = gout ? launch_fwd_tma<T, IdxT, false, true>(a, s) : launch_fwd_tma<T, IdxT, false, false>(a, s);
+    return rc > 0 ? ASCAN_OK : (rc == 0 ? ASCAN_EINVAL : rc);
+  }
   if (vec && use_tma() && a.N >= tma::Fmt<T>::kElemsPerRow) {
     int rc;
     if (reverse)
@@ -1192,7 +1249,8 @@ static void bwd_dispatch(const BwdArgs<T, IdxT>& a, bool causal, cudaStream_t s)
 template <typename T, typename IdxT>
 static int bwd_typed(const void* dy, const void* g, const void* h, void* dx, void* dg,
                      const void* cu, int64_t S, int64_t C, int64_t BL, int causal,
-                     const Workspace& w, cudaStream_t s) {
+                     const Workspace& w, cudaStream_t s,
+                     const RowIO& io = RowIO{nullptr, nullptr, nullptr}) {
   BwdArgs<T, IdxT> a;
   a.dy = static_cast<const T*>(dy);
   a.g = static_cast<const T*>(g);
@@ -1206,8 +1264,16 @@ static int bwd_typed(const void* dy, const void* g, const void* h, void* dx, voi
   a.num_tiles = static_cast<uint32_t>(tiles_of(a.N));
   a.ticket = w.ticket;
   a.st = w.st;
+  a.io = io;
   const bool vec = aligned16(dy) && aligned16(g) && aligned16(h) && aligned16(dx) && aligned16(dg);
   constexpr int kVec = 16 / sizeof(T);
+  // row I/O and absent outputs exist only in the persistent TMA kernels
+  const bool slab = io.carry || io.halo || io.agg || !dx;
+  if (slab) {
+    if (!vec || a.N < tma::Fmt<T>::kElemsPerRow) return ASCAN_EINVAL;
+    const int rc = causal ? launch_bwd_tma<T, IdxT, true>(a, s) : launch_bwd_tma<T, IdxT, false>(a, s);
+    return rc > 0 ? ASCAN_OK : (rc == 0 ? ASCAN_EINVAL : rc);
+  }
   if (vec && use_tma() && a.N >= tma::Fmt<T>::kElemsPerRow) {
     const int rc = causal ? launch_bwd_tma<T, IdxT, true>(a, s) : launch_bwd_tma<T, IdxT, false>(a, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
@@ -1332,6 +1398,58 @@ int ascan_backward(const void* grad, const void* gates, const void* states, void
 #define ASCAN_BWD_CALL(T, I)                                                                    \
   bwd_typed<T, I>(grad, gates, states, d_tokens, d_gates, cu_seqlens, num_seq, num_channels,    \
                   seq_total, causal, w, s)
+  ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_BWD_CALL);
+#undef ASCAN_BWD_CALL
+}
+
+int ascan_forward_slab(const void* gates, const void* tokens, void* tokens_out, void* gates_out,
+                       const void* cu_seqlens, int cu_index_type, int64_t num_seq,
+                       int64_t num_channels, int64_t seq_total, int dtype, int reverse,
+                       const float* row_carry, float* row_aggregate, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  int rc = check_common(cu_seqlens, cu_index_type, num_seq, num_channels, seq_total, dtype);
+  if (rc != ASCAN_OK) return rc;
+  if (!gates || !tokens) return ASCAN_EINVAL;
+  if (!tokens_out && (gates_out || !row_aggregate)) return ASCAN_EINVAL;
+  const int64_t n = num_channels * seq_total;
+  if (n == 0 || num_seq == 0) return ASCAN_OK;
+  Workspace w;
+  rc = carve(workspace, workspace_bytes, n, w);
+  if (rc != ASCAN_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(w.ticket, 0, w.clear_bytes, s) != cudaSuccess) return ASCAN_ECUDA;
+  const RowIO io{row_carry, nullptr, row_aggregate};
+#define ASCAN_FWD_CALL(T, I)                                                                   \
+  fwd_typed<T, I>(gates, tokens, tokens_out, gates_out, cu_seqlens, num_seq, num_channels,     \
+                  seq_total, reverse, w, s, io)
+  ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_FWD_CALL);
+#undef ASCAN_FWD_CALL
+}
+
+int ascan_backward_slab(const void* grad, const void* gates, const void* states, void* d_tokens,
+                        void* d_gates, const void* cu_seqlens, int cu_index_type, int64_t num_seq,
+                        int64_t num_channels, int64_t seq_total, int dtype, int causal,
+                        const float* row_carry, const float* row_state_halo, float* row_aggregate,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_common(cu_seqlens, cu_index_type, num_seq, num_channels, seq_total, dtype);
+  if (rc != ASCAN_OK) return rc;
+  if (!grad || !gates || !states) return ASCAN_EINVAL;
+  if ((d_tokens == nullptr) != (d_gates == nullptr)) return ASCAN_EINVAL;
+  if (!d_tokens && !row_aggregate) return ASCAN_EINVAL;
+  if (d_tokens && (d_gates == gates || d_gates == states || d_tokens == gates ||
+                   d_tokens == states || d_tokens == d_gates))
+    return ASCAN_EINVAL;
+  const int64_t n = num_channels * seq_total;
+  if (n == 0 || num_seq == 0) return ASCAN_OK;
+  Workspace w;
+  rc = carve(workspace, workspace_bytes, n, w);
+  if (rc != ASCAN_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(w.ticket, 0, w.clear_bytes, s) != cudaSuccess) return ASCAN_ECUDA;
+  const RowIO io{row_carry, row_state_halo, row_aggregate};
+#define ASCAN_BWD_CALL(T, I)                                                                    \
+  bwd_typed<T, I>(grad, gates, states, d_tokens, d_gates, cu_seqlens, num_seq, num_channels,    \
+                  seq_total, causal, w, s, io)
   ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_BWD_CALL);
 #undef ASCAN_BWD_CALL
 }

@@ -472,6 +472,95 @@ __device__ __forceinline__ uint32_t carry_mask(uint32_t head) {
   return 0xffffu & ~((2u << (31 - __clz(head))) - 1u);
 }
 
+// ---- time slabs: per-row carry-in, halo and aggregate --------------------
+
+// Row index of flat position q when q sits at row position `want`, else -1.
+__device__ __forceinline__ int64_t row_at(int64_t q, int64_t BL, int64_t want) {
+  const int64_t r = q / BL;
+  return q - r * BL == want ? r : -1;
+}
+
+// Forward: the carried (gate product, state) of each row enters at the row's
+// first element in scan order, which is a sequence head: x' = x + g * state
+// and g' = g * product reproduce the continued recurrence and its gate
+// products exactly.  `bits` holds the thread's heads.
+template <bool REV>
+__device__ __forceinline__ void apply_row_carry(float (&a)[kPerThread], float (&b)[kPerThread],
+                                                uint32_t bits, int64_t p, int64_t BL,
+                                                const float* carry) {
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    if ((bits >> j) & 1u) {
+      const int64_t r = row_at(p + j, BL, REV ? BL - 1 : 0);
+      if (r >= 0) {
+        b[j] = fmaf(a[j], carry[2 * r + 1], b[j]);
+        a[j] *= carry[2 * r];
+      }
+    }
+  }
+}
+
+// Backward: the carried adjoint term enters at the row's first element in
+// scan order (a head: the end of the slab's last sequence piece); its
+// successor gate lives outside the slab and is already part of the term, so
+// the element's own coefficient becomes the identity.
+template <bool CAUSAL>
+__device__ __forceinline__ void apply_row_carry_adjoint(float (&a)[kPerThread],
+                                                        float (&b)[kPerThread], uint32_t bits,
+                                                        int64_t p, int64_t BL, const float* carry) {
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    if ((bits >> j) & 1u) {
+      const int64_t r = row_at(p + j, BL, CAUSAL ? BL - 1 : 0);
+      if (r >= 0) {
+        b[j] += carry[r];
+        a[j] = 1.f;
+      }
+    }
+  }
+}
+
+// Backward: the state neighbour of the row element whose neighbour lies
+// outside the slab.  Returns the bits that took a halo (their gate gradient
+// is not forced to zero).
+template <bool CAUSAL>
+__device__ __forceinline__ uint32_t apply_row_halo(float (&hv)[kPerThread], uint32_t bits,
+                                                   int64_t p, int64_t BL, const float* halo) {
+  uint32_t used = 0u;
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    if ((bits >> j) & 1u) {
+      const int64_t r = row_at(p + j, BL, CAUSAL ? 0 : BL - 1);
+      if (r >= 0) {
+        hv[j] = halo[r];
+        used |= 1u << j;
+      }
+    }
+  }
+  return used;
+}
+
+// Inclusive (gate product, value) at each row's last element in scan order.
+// a, b are the thread's local prefixes and P its exclusive prefix; elements in
+// `cm` (before the thread's first head) take P.
+template <bool REV>
+__device__ __forceinline__ void record_row_agg(const float (&a)[kPerThread],
+                                               const float (&b)[kPerThread], uint32_t bits,
+                                               uint32_t cm, const Pfx& P, int64_t p, int64_t BL,
+                                               float* agg) {
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    if ((bits >> j) & 1u) {
+      const int64_t r = row_at(p + j, BL, REV ? 0 : BL - 1);
+      if (r >= 0) {
+        const bool c = (cm >> j) & 1u;
+        agg[2 * r] = c ? a[j] * P.a : a[j];
+        agg[2 * r + 1] = c ? fmaf(a[j], P.b, b[j]) : b[j];
+      }
+    }
+  }
+}
+
 // Slot hand-off in shared memory: value words, fence, then the tag.
 __device__ __forceinline__ void xs_put(float4* slot, const Pfx& p, uint32_t tag) {
   volatile float* v = reinterpret_cast<volatile float*>(slot);

@@ -153,6 +153,55 @@ ASCAN_API int ascan_forward_noalloc(const void* gates, const void* tokens, void*
                                     int dtype, int reverse, void* stream);
 
 /*
+ * Time slabs: the scan of columns [t0, t1) of every row when the sequence
+ * axis of a longer problem is split across devices (the rest of each row
+ * lives on other GPUs).  No counterpart in the reference, whose kernels see
+ * whole rows; these entry points serve a time-sharded run (reduce, exchange a
+ * few floats per row, scan again), see associative_scan_triton/time_shard.py.
+ *
+ * cu_seqlens are the slab's own boundaries rebased to the slab (cu[0] = 0,
+ * cu[S] = seq_total): the slab's first piece may continue a sequence that
+ * started on an earlier device, and its last piece may go on after it.
+ * All pointers must be 16-byte aligned and the slab must hold at least one
+ * 128-byte row; otherwise ASCAN_EINVAL.  Per-row arrays are float32, indexed
+ * by channel, in device memory.
+ *
+ * ascan_forward_slab: ascan_forward plus
+ *   row_carry     [C][2] (gate product, state) that enters each row's first
+ *                 element in scan order (NULL: none, as ascan_forward);
+ *   row_aggregate [C][2] output: the inclusive (gate product, state) at each
+ *                 row's last element in scan order (NULL: not written).
+ *   tokens_out may be NULL together with gates_out for an aggregate-only pass
+ *   (reads gates and tokens, writes only row_aggregate).
+ * ascan_backward_slab: ascan_backward plus
+ *   row_carry      [C] additive term for the adjoint at each row's first
+ *                  element in scan order (causal: the slab's last column):
+ *                  the successor gate times the successor adjoint, both from
+ *                  the neighbouring slab (NULL: none);
+ *   row_state_halo [C] state neighbour of the element whose neighbour lies
+ *                  outside the slab (causal: h[t0-1], anti-causal: h[t1]);
+ *                  that element's gate gradient uses it instead of being
+ *                  zero at a sequence start (NULL: as ascan_backward);
+ *   row_aggregate  [C][2] output: inclusive (coefficient product, adjoint) at
+ *                  each row's last element in scan order, where the product
+ *                  leaves out the first element's coefficient (it lives in
+ *                  row_carry).
+ *   d_tokens and d_gates may both be NULL for an aggregate-only pass.
+ */
+ASCAN_API int ascan_forward_slab(const void* gates, const void* tokens, void* tokens_out,
+                                 void* gates_out, const void* cu_seqlens, int cu_index_type,
+                                 int64_t num_seq, int64_t num_channels, int64_t seq_total,
+                                 int dtype, int reverse, const float* row_carry,
+                                 float* row_aggregate, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+ASCAN_API int ascan_backward_slab(const void* grad, const void* gates, const void* states,
+                                  void* d_tokens, void* d_gates, const void* cu_seqlens,
+                                  int cu_index_type, int64_t num_seq, int64_t num_channels,
+                                  int64_t seq_total, int dtype, int causal, const float* row_carry,
+                                  const float* row_state_halo, float* row_aggregate,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Shift by one position inside every sequence and pad the vacated slot.
  * Replaces _shift_pad_kernel / shift_pad_compiled
  * (src/associative_scan_triton/_shift_pad.py:63-165) and the torch.roll

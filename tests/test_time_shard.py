@@ -1,0 +1,234 @@
+"""Time-sharded causal scan: slabs of one long sequence axis.
+
+GPU tests run every slab of a problem on one device through the same passes
+and carry folds as the multi-rank driver (``emulate_forward`` /
+``emulate_backward``) and compare the concatenated slabs with the fp64 oracle
+on the whole axis.  CPU tests run the exchange and the folds as 2-4 ``gloo``
+ranks on aggregates computed in numpy from their definitions, and check the
+carries against the oracle's states at the slab edges.  A real multi-GPU run
+(NCCL, one rank per GPU) is ``test_nccl_ranks_match_oracle`` and needs at
+least two GPUs.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from associative_scan_triton import time_shard as ts
+from oracle import oracle
+from scan_testlib import assert_close_to_gold, make_inputs
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+# --- host geometry ---------------------------------------------------------------------
+
+def test_plan_slabs_rebases_boundaries():
+  plans = ts.plan_slabs([0, 100, 256, 300, 512], [0, 256, 512])
+  assert plans[0].local_cu == (0, 100, 256) and plans[0].starts_new and plans[0].inner_boundary
+  assert plans[1].local_cu == (0, 44, 256) and plans[1].starts_new and plans[1].inner_boundary
+  one = ts.plan_slabs([0, 1000], [0, 256, 512, 1000])
+  assert [p.starts_new for p in one] == [True, False, False]
+  assert [p.last_piece_continues for p in one] == [False, True, True]
+  with pytest.raises(ValueError):
+    ts.plan_slabs([0, 5, 3, 10], [0, 10])
+  with pytest.raises(ValueError):
+    ts.plan_slabs([0, 10], [0, 4, 4, 10])
+
+
+def test_even_bounds():
+  assert ts.even_bounds(1 << 20, 8) == [k * (1 << 17) for k in range(9)]
+  b = ts.even_bounds(1000, 3, align=8)
+  assert b[0] == 0 and b[-1] == 1000 and all(x % 8 == 0 for x in b[:-1])
+  with pytest.raises(ValueError):
+    ts.even_bounds(10, 4, align=8)
+
+
+# --- numpy definitions of the per-slab records (fp64) ----------------------------------
+
+def _fwd_aggregate(g, x, plan):
+  """(P, Y) per row: gate product since the last local boundary, state from 0."""
+  C, L = g.shape
+  last = max(b for b in plan.local_cu if b < L)
+  P = np.prod(g[:, last:], axis=1)
+  y = np.zeros(C)
+  for t in range(last, L):
+    y = g[:, t] * y + x[:, t]
+  return np.stack([P, y], axis=1)
+
+
+def _bwd_aggregate(dy, g, plan):
+  """(Q, D) per row at column 0 from a zero carry: the adjoint and the product
+  of the coefficients g[t+1] since the nearest sequence end at or after it
+  (that end's own coefficient included; the slab's last column counts 1)."""
+  C, L = g.shape
+  ends = {b - 1 for b in plan.local_cu[1:]}
+  dh = np.zeros(C)
+  q = np.ones(C)
+  for t in range(L - 1, -1, -1):
+    coeff = g[:, t + 1] if t + 1 < L else np.ones(C)
+    if t in ends:  # a sequence ends at t: the recurrence restarts
+      dh = dy[:, t].copy()
+      q = coeff.copy()
+    else:
+      dh = dy[:, t] + coeff * dh
+      q = q * coeff
+  return np.stack([q, dh], axis=1)
+
+
+def _protocol_worker(rank, world, port, C, T, cu, seed, errq):
+  import torch.distributed as dist
+  try:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    rng = np.random.default_rng(seed)
+    g = rng.uniform(0.9, 1.0, size=(C, T))
+    x = rng.standard_normal((C, T))
+    dy = rng.standard_normal((C, T))
+    bounds = ts.even_bounds(T, world, align=8)
+    plans = ts.plan_slabs(cu, bounds)
+    t0, t1 = bounds[rank], bounds[rank + 1]
+    gather = ts._all_gather
+    agg = torch.from_numpy(_fwd_aggregate(g[:, t0:t1], x[:, t0:t1], plans[rank]))
+    carry = ts.forward_carry(plans, gather(agg), rank)
+    bagg = torch.from_numpy(_bwd_aggregate(dy[:, t0:t1], g[:, t0:t1], plans[rank]))
+    firsts = [r.reshape(-1) for r in gather(torch.from_numpy(g[:, t0].copy()))]
+    bcarry = ts.backward_carry(plans, gather(bagg), firsts, rank)
+    # oracle on the whole axis: the state before t0 and the adjoint after t1
+    cu_t = torch.tensor(cu, dtype=torch.int64)
+    y_full, a_full = oracle.scan_fwd(torch.from_numpy(g).float(), torch.from_numpy(x).float(), cu_t)
+    h_prev = y_full[:, t0 - 1] if (rank > 0 and not plans[rank].starts_new) else np.zeros(C)
+    np.testing.assert_allclose(carry[:, 1].numpy(), h_prev, rtol=1e-5, atol=1e-5)
+    if rank > 0 and not plans[rank].starts_new:
+      np.testing.assert_allclose(carry[:, 0].numpy(), a_full[:, t0 - 1], rtol=1e-5, atol=1e-12)
+    dx_full, _ = oracle.scan_bwd(torch.from_numpy(dy).float(), torch.from_numpy(g).float(),
+                                 torch.from_numpy(y_full).float(), cu_t)
+    if rank < world - 1 and not plans[rank + 1].starts_new:
+      want = g[:, t1].astype(np.float32).astype(np.float64) * dx_full[:, t1]
+    else:
+      want = np.zeros(C)
+    np.testing.assert_allclose(bcarry.numpy(), want, rtol=1e-5, atol=1e-5)
+    dist.destroy_process_group()
+  except BaseException as e:  # reported to the parent
+    errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+    raise
+
+
+def _free_port() -> int:
+  with socket.socket() as s:
+    s.bind(("127.0.0.1", 0))
+    return s.getsockname()[1]
+
+
+@pytest.mark.parametrize(("world", "cu"), [
+  (2, [0, 512]),                       # one sequence across both slabs
+  (4, [0, 512]),
+  (4, [0, 100, 128, 300, 512]),        # boundaries inside slabs and on a slab edge
+  (3, [0, 17, 400, 401, 512]),
+])
+def test_exchange_and_folds_on_gloo_ranks(world, cu):
+  import multiprocessing as mp
+  ctx = mp.get_context("spawn")
+  errq = ctx.Queue()
+  port = _free_port()
+  procs = [ctx.Process(target=_protocol_worker, args=(r, world, port, 3, 512, cu, 7, errq))
+           for r in range(world)]
+  for p in procs:
+    p.start()
+  for p in procs:
+    p.join(timeout=120)
+  errors = []
+  while not errq.empty():
+    errors.append(errq.get())
+  for p in procs:
+    if p.is_alive():
+      p.kill()
+      errors.append("a rank did not finish")
+  assert not errors and all(p.exitcode == 0 for p in procs), errors
+
+
+# --- GPU: emulated slabs against the oracle on the whole axis ---------------------------
+
+CASES = [
+  # C, T, world, cu_seqlens
+  (8, 1 << 16, 4, [0, 1 << 16]),                       # one long sequence (the 5b shape, small)
+  (4, 1 << 15, 8, [0, 1 << 15]),
+  (5, 3 * 4096 * 4, 4, [0, 5000, 12288, 20000, 49152]),  # boundaries inside, one on an edge
+  (3, 8192 * 3, 3, [0, 1, 8191, 8192, 24575, 24576]),   # pieces of one element at the edges
+  (2, 4096 * 6 + 64, 5, [0, 4096 * 6 + 64]),            # slabs not multiples of a tile
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(("C", "T", "world", "cu"), CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_emulated_slabs_match_oracle(C, T, world, cu, dtype):
+  g, x = make_inputs(C, T, dtype=dtype, gate="verylong", seed=C + T + world)
+  dy = torch.randn(C, T, generator=torch.Generator().manual_seed(3)).to("cuda", dtype)
+  bounds = ts.even_bounds(T, world, align=64)
+  plans = ts.plan_slabs(cu, bounds)
+  sl = [slice(a, b) for a, b in zip(bounds, bounds[1:])]
+  gs = [g[:, s].contiguous() for s in sl]
+  xs = [x[:, s].contiguous() for s in sl]
+  dys = [dy[:, s].contiguous() for s in sl]
+  ys = ts.emulate_forward(gs, xs, plans)
+  y = torch.cat(ys, dim=1)
+  cu_t = torch.tensor(cu, dtype=torch.int64, device="cuda")
+  gold_y, _ = oracle.scan_fwd(g, x, cu_t)
+  assert_close_to_gold(y, gold_y, dtype, "time-sharded y")
+  grads = ts.emulate_backward(dys, gs, ys, plans)
+  dg = torch.cat([d[0] for d in grads], dim=1)
+  dx = torch.cat([d[1] for d in grads], dim=1)
+  gdx, gdg = oracle.scan_bwd(dy, g, y, cu_t)
+  assert_close_to_gold(dx, gdx, dtype, "time-sharded dx")
+  assert_close_to_gold(dg, gdg, dtype, "time-sharded dg")
+
+
+@pytest.mark.gpu
+def test_slab_aggregate_matches_definition():
+  C, T = 6, 4096 * 2 + 128
+  g, x = make_inputs(C, T, gate="long", seed=11)
+  plan = ts.plan_slabs([0, 3000, T], [0, T])[0]
+  agg = ts.slab_forward_aggregate(g, x, plan)
+  want = _fwd_aggregate(g.double().cpu().numpy(), x.double().cpu().numpy(), plan)
+  np.testing.assert_allclose(agg.cpu().numpy(), want, rtol=1e-5, atol=1e-6)
+  dy = torch.randn_like(x)
+  h = torch.randn_like(x)
+  bagg = ts.slab_backward_aggregate(dy, g, h, plan)
+  bwant = _bwd_aggregate(dy.double().cpu().numpy(), g.double().cpu().numpy(), plan)
+  np.testing.assert_allclose(bagg.cpu().numpy(), bwant, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.gpu
+def test_slab_entry_points_refuse_unaligned_views():
+  from associative_scan_triton import _lib
+  C, L = 2, 1024
+  base = torch.rand(C * L + 1, device="cuda")
+  g = base[1:].view(C, L)  # 4-byte offset: not 16-byte aligned
+  x = torch.rand(C, L, device="cuda")
+  cu = torch.tensor([0, L], device="cuda")
+  agg = torch.empty(C, 2, device="cuda")
+  with pytest.raises(_lib.ScanError, match="invalid"):
+    _lib.forward_slab(g, x, None, None, cu, 1, C, False, row_aggregate=agg)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_ranks_match_oracle(tmp_path):
+  world = min(torch.cuda.device_count(), 4)
+  script = REPO / "tests" / "time_shard_ranks.py"
+  cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+         "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(script),
+         str(tmp_path)]
+  env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+  r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
+  assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+  assert (tmp_path / "ok").read_text().strip() == str(world)
