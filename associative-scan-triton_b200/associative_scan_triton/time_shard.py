@@ -154,8 +154,20 @@ def state_halo(plans: Sequence[SlabPlan], last_states: Sequence[torch.Tensor],
 # per-slab passes (one GPU, one slab)
 # ---------------------------------------------------------------------------
 
+_CU_CACHE: dict[tuple, torch.Tensor] = {}
+
+
 def _cu_tensor(plan: SlabPlan, device) -> torch.Tensor:
-  return torch.tensor(plan.local_cu, dtype=torch.int64, device=device)
+  """The slab's rebased boundaries on the device, uploaded once per plan (a
+  fresh upload from pageable memory would synchronise every pass)."""
+  key = (plan.local_cu, str(torch.device(device)))
+  t = _CU_CACHE.get(key)
+  if t is None:
+    if len(_CU_CACHE) > 256:
+      _CU_CACHE.clear()
+    t = torch.tensor(plan.local_cu, dtype=torch.int64, device=device)
+    _CU_CACHE[key] = t
+  return t
 
 
 def slab_forward_aggregate(gates: torch.Tensor, tokens: torch.Tensor,

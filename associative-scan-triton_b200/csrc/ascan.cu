@@ -439,7 +439,8 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
                                              const CUtensorMap* const* maps,
                                              const tma::CuView<IdxT>& cu, int64_t N,
                                              int64_t n_tma_total, const tma::TileSched& sch,
-                                             const TileStatus& st, int lane, Extra extra) {
+                                             const TileStatus& st, int lane, Extra extra,
+                                             int n_load = NIN) {
   using namespace tma;
   if (lane == 0)
     for (int k = 0; k < NIN; ++k) prefetch_map(maps[k]);
@@ -510,8 +511,9 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
     if (lane == 0) {
       m.ticket = ticket;
       if (!read_pred) m.te_raw[1] = m.te_raw[3] = kStatusNone;
-      mbar_expect_tx(&sm.full[stage], NIN * Fmt<T>::kBytes + (read_pred ? 16u : 0u));
-      for (int k = 0; k < NIN; ++k) tma_load_2d(sm.in[stage][k], maps[k], 0, row, &sm.full[stage]);
+      // the first n_load inputs (an aggregate-only backward skips the states)
+      mbar_expect_tx(&sm.full[stage], n_load * Fmt<T>::kBytes + (read_pred ? 16u : 0u));
+      for (int k = 0; k < n_load; ++k) tma_load_2d(sm.in[stage][k], maps[k], 0, row, &sm.full[stage]);
       if (read_pred) bulk_load(m.te_raw, st.slots + (ticket - sch.stride), 16u, &sm.full[stage]);
     }
     pending[stage] = true;
@@ -625,8 +627,13 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
     const uint32_t omask = has_outside ? (m.obits[bit_word] >> bit_shift) & 0xffffu : 0u;
     const bool first_is_head =
         REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
-    const bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
-    const Pfx te_meta{__uint_as_float(m.te_raw[0]), __uint_as_float(m.te_raw[2]), kValid};
+    bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
+    Pfx te_meta{__uint_as_float(m.te_raw[0]), __uint_as_float(m.te_raw[2]), kValid};
+    // the scan-first warp re-reads its predecessor now, while it folds the tile
+    const bool early = (REV ? kConsumerWarps - 1 - warp : warp) == 0 && !te_known &&
+                       !first_is_head && ticket >= sch.stride;
+    uint4 early_raw = make_uint4(0u, 0u, 0u, 0u);
+    if (early && lane == 0) early_raw = load_status_raw(args.st, ticket - sch.stride);
     // time slabs: row ends in scan order, where the row aggregate is taken
     const uint32_t lastmask =
         IO && args.io.agg ? ((REV ? m.sbits[bit_word] : m.ebits[bit_word]) >> bit_shift) & 0xffffu
@@ -642,6 +649,7 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
 
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(a, b, head), lane, ex, wtot);
+    if (early) take_early(early_raw, te_known, te_meta);
     const Pfx P = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
                                         sch.stride, te_known, te_meta, warp, lane, ok);
     // a, b hold the local prefixes: h = A_loc * carry + B_loc before the first head
@@ -774,7 +782,8 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
             if (bulk & (1u << kn)) bulk_load(m.halo_raw[kn], arr[kn] + pn, 16u, bar);
             if (bulk & (1u << kp)) bulk_load(m.halo_raw[kp], arr[kp] + (p0 - V), 16u, bar);
           }
-        });
+        },
+        IO && args.dx == nullptr ? 2 : NIN);  // aggregate-only: the states are never read
     return;
   }
 
@@ -830,8 +839,13 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
     const uint32_t omask = has_outside ? (m.obits[bit_word] >> bit_shift) & 0xffffu : 0u;
     const bool first_is_head =
         REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
-    const bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
-    const Pfx te_meta{__uint_as_float(m.te_raw[0]), __uint_as_float(m.te_raw[2]), kValid};
+    bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
+    Pfx te_meta{__uint_as_float(m.te_raw[0]), __uint_as_float(m.te_raw[2]), kValid};
+    // the scan-first warp re-reads its predecessor now, while it folds the tile
+    const bool early = (REV ? kConsumerWarps - 1 - warp : warp) == 0 && !te_known &&
+                       !first_is_head && ticket >= sch.stride;
+    uint4 early_raw = make_uint4(0u, 0u, 0u, 0u);
+    if (early && lane == 0) early_raw = load_status_raw(args.st, ticket - sch.stride);
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[stage]);
     if (++stage == NS) {
@@ -866,6 +880,7 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
       tail &= ~apply_row_halo<CAUSAL>(hv, tail, p0 + o, BL, args.io.halo);
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(gv, dyv, head), lane, ex, wtot);
+    if (early) take_early(early_raw, te_known, te_meta);
     const Pfx P = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
                                         sch.stride, te_known, te_meta, warp, lane, ok);
     // gv, dyv hold the local prefixes: dh = A_loc * carry + B_loc before the first head
@@ -1100,23 +1115,21 @@ static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles,
 // and at least two waves of rows, so that a tile's predecessor is old enough
 // to be read ahead.
 // Tile order of the TMA kernels: row mode needs row-aligned tiles (BL a
-// multiple of the tile) and pays off when sequences span several tiles (in
+// multiple of the tile) and pays off when sequences span several tiles: in
 // flat order their tiles are consecutive tickets of one wave, so every tile
-// waits for the one before it) and a tile's row predecessor is at least two
-// waves older (rows >= 2 x CTAs).  When sequences fit in a tile on average,
+// waits on a look-back behind the one before it, while in row order a tile's
+// predecessor is `rows` tickets older (many waves when rows >> CTAs, and
+// never closer than in flat order).  When sequences fit in a tile on average,
 // the flat order is slightly faster (a wave reads one contiguous range).
 // Implementations 3 and 4 force the flat and the row order; both orders give
 // the same results up to floating-point reassociation.
 static tma::TileSched make_sched(uint32_t num_tiles, int64_t N, int64_t BL, int64_t S) {
   tma::TileSched sch{num_tiles, 0u, 0u, 0u, 1u};
   const int64_t C = BL > 0 ? N / BL : 0;
-  const int sms = sm_count();
   const int mode = impl_mode();
   const bool fits = BL % kTile == 0 && C >= 1 && C <= 0x7fffffffll;
   const bool long_seqs = BL > S * static_cast<int64_t>(kTile);  // mean length above a tile
-  const bool row = mode == 4   ? fits
-                   : mode == 3 ? false
-                               : fits && long_seqs && sms > 0 && C >= 2ll * sms;
+  const bool row = mode == 4 ? fits : mode == 3 ? false : fits && long_seqs;
   if (row) {
     sch.row_mode = 1u;
     sch.rows = static_cast<uint32_t>(C);

@@ -561,6 +561,29 @@ __device__ __forceinline__ void record_row_agg(const float (&a)[kPerThread],
   }
 }
 
+// The scan-first warp's early read of its tile's predecessor status: issued
+// by lane 0 when the tile starts, so that its round trip overlaps the tile's
+// local fold and warp scan; take_early() turns an inclusive record into the
+// known carry-in (otherwise the warp looks back as usual).
+__device__ __forceinline__ uint4 load_status_raw(const TileStatus& st, uint32_t q) {
+  uint4 r;
+  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(st.slots + q)
+               : "memory");
+  return r;
+}
+
+// Warp-wide (all lanes call): adopt lane 0's early record if it is inclusive.
+__device__ __forceinline__ void take_early(const uint4& raw, bool& te_known, Pfx& te) {
+  const uint32_t k1 = __shfl_sync(kFull, raw.y, 0), k3 = __shfl_sync(kFull, raw.w, 0);
+  const uint32_t a = __shfl_sync(kFull, raw.x, 0), b = __shfl_sync(kFull, raw.z, 0);
+  if (k1 == kStatusInclusive && k3 == kStatusInclusive) {
+    te_known = true;
+    te = Pfx{__uint_as_float(a), __uint_as_float(b), kValid};
+  }
+}
+
 // Slot hand-off in shared memory: value words, fence, then the tag.
 __device__ __forceinline__ void xs_put(float4* slot, const Pfx& p, uint32_t tag) {
   volatile float* v = reinterpret_cast<volatile float*>(slot);

@@ -252,6 +252,72 @@ def _e2e(ast, device, g_dev, x_dev, dy_dev, cu, steps: int) -> dict:
           "d2h_bytes_per_step": 3 * n * 4, "n": n}
 
 
+TS_C, TS_T = 256, 1 << 20  # configs[4] time-shard: one sequence of 2^20 steps, 256 channels
+
+
+def _time_shard_5b(dist, rank: int, world: int, device, steps: int = 10) -> dict:
+  """configs[4]'s time-sharded case: C=256 channels of one sequence of T=2^20
+  fp32 steps, gates ~ U(0.99, 1); rank k scans columns [kT/W, (k+1)T/W) and
+  exchanges per-row carries once per direction (NCCL all-gather).  At W=1 the
+  same workload runs as an ordinary single-GPU scan.  Device time per
+  fwd+bwd step, max over ranks; GB/s counts the single-device algorithmic
+  bytes (32 B per element), so the second reads of the two passes show up as
+  a lower rate."""
+  import associative_scan_triton as ast
+  from associative_scan_triton import time_shard as ts
+  bounds = ts.even_bounds(TS_T, world, align=64)
+  t0, t1 = bounds[rank], bounds[rank + 1]
+  gen = torch.Generator(device=device).manual_seed(99 + rank)
+  L = t1 - t0
+  g = 0.99 + 0.01 * torch.rand(TS_C, L, device=device, generator=gen)
+  x = torch.randn(TS_C, L, device=device, generator=gen)
+  dy = torch.randn(TS_C, L, device=device, generator=gen)
+  plans = ts.plan_slabs([0, TS_T], bounds)
+  gather = ts._all_gather
+  if world > 1:
+    def fwd():
+      return ts.time_sharded_forward(g, x, plans, rank, gather)
+
+    def bwd(y):
+      return ts.time_sharded_backward(dy, g, y, plans, rank, gather)
+  else:
+    cu = torch.tensor([0, TS_T], dtype=torch.int32, device=device)
+    grid = (1, 1, TS_C)
+    y1, dx1, dg1 = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+
+    def fwd():
+      ast.forward_scan_full(g, x, cu, grid, REVERSE=False, CHUNK_SIZE=512, TESTING=False,
+                            tokens_out=y1)
+      return y1
+
+    def bwd(y):
+      ast.backward_scan_fused_full(dy, g, y, dx1, dg1, cu, grid, CHUNK_SIZE=512, CAUSAL=True)
+  for _ in range(3):
+    bwd(fwd())
+  torch.cuda.synchronize()
+  _barrier(dist, device)
+  marks = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+  start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  start.record()
+  for i in range(steps):
+    marks[i][0].record()
+    ys = fwd()
+    marks[i][1].record()
+    bwd(ys)
+  stop.record()
+  torch.cuda.synchronize()
+  _barrier(dist, device)
+  step_ms = _max_over_ranks(dist, start.elapsed_time(stop) / steps, device)
+  fwd_ms = _max_over_ranks(dist, sum(a.elapsed_time(b) for a, b in marks) / steps, device)
+  n = TS_C * TS_T
+  return {"workload": f"causal fwd+bwd, C={TS_C}, one sequence of T=2^20, fp32, "
+                      f"time-sharded over {world} GPU(s) (configs[4])",
+          "ms_per_step": round(step_ms, 4), "fwd_ms": round(fwd_ms, 4),
+          "gbs": round(STEP_BYTES_PER_ELEM * n / (step_ms * 1e-3) / 1e9, 1),
+          "exchange": "one NCCL all-gather of [C,2] (fwd) and [C,4] (bwd) floats per step"
+                      if world > 1 else "none (single GPU)"}
+
+
 def _cpu_baseline(seconds: float = 10.0) -> dict:
   """The reference's CPU algorithm (fp64 sequential scan, oracle port) on a channel sample."""
   from oracle import oracle
@@ -338,6 +404,9 @@ def run_ours(args) -> dict | None:
   e2e_steps = max(3, min(args.steps, 10))
   e2e = _e2e(ast, device, g, x, dy, cu, e2e_steps)
   e2e_ms = _max_over_ranks(dist, e2e["ms_per_step"], device)
+  del g, x, dy, y, dx, dg
+  torch.cuda.empty_cache()
+  time_shard = None if args.no_time_shard else _time_shard_5b(dist, rank, world, device)
 
   if dist is not None:
     _barrier(dist, device)
@@ -391,6 +460,8 @@ def run_ours(args) -> dict | None:
     "gpu_launches": 2 * args.steps,
     "clocks": clocks,
   }
+  if time_shard is not None:
+    line["time_shard"] = time_shard
   if not args.no_sweep and world == 1:
     line["sweep_B8_C1536_fp32"] = _sweep(ast, device)
   if not args.no_cpu_baseline and world == 1:
@@ -474,6 +545,7 @@ def main(argv=None) -> int:
   ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
   ap.add_argument("--no-sweep", action="store_true")
   ap.add_argument("--no-cpu-baseline", action="store_true")
+  ap.add_argument("--no-time-shard", action="store_true")
   ap.add_argument("--cpu-seconds", type=float, default=10.0)
   args = ap.parse_args(argv)
   args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
