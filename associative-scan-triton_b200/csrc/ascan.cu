@@ -412,7 +412,9 @@ namespace ascan {
 
 // Stages of the input ring: the deepest ring (at most 6) that fits next to the
 // output staging buffers in the 227 KB of shared memory a CTA may use.
-constexpr size_t kSmemBudget = 227 * 1024;
+// Shared memory of one persistent CTA: the SM's 228 KB shared by kCtasPerSm
+// CTAs, 1 KB of each reserved by the hardware.
+constexpr size_t kSmemBudget = (228 * 1024) / tma::kCtasPerSm - 1024;
 
 template <typename T, int NIN, int NOUT, int NS = 6>
 constexpr int ring_depth() {
@@ -551,7 +553,7 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
 // IO: the launch serves a time slab (RowIO in use or no outputs); compiled
 // separately so the ordinary kernels carry none of that code.
 template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO>
-__global__ void __launch_bounds__(tma::kThreads, 1)
+__global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     scan_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_g,
                         const __grid_constant__ CUtensorMap map_x,
                         const __grid_constant__ CUtensorMap map_y,
@@ -710,7 +712,7 @@ __global__ void __launch_bounds__(tma::kThreads, 1)
 }
 
 template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO>
-__global__ void __launch_bounds__(tma::kThreads, 1)
+__global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     scan_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dy,
                         const __grid_constant__ CUtensorMap map_g,
                         const __grid_constant__ CUtensorMap map_h,
@@ -985,17 +987,23 @@ struct Workspace {
 
 static size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
+// Tiles of the plain kernels (kTile elements) and of the persistent TMA
+// kernels (tma::kTileElems, a divisor of kTile); status slots are counted in
+// the smaller tiles so that either family fits the same workspace.
 static size_t tiles_of(int64_t n) { return static_cast<size_t>((n + kTile - 1) / kTile); }
+static size_t tma_tiles_of(int64_t n) {
+  return static_cast<size_t>((n + tma::kTileElems - 1) / tma::kTileElems);
+}
+static size_t status_slots(int64_t n) { return tma_tiles_of(n); }
 
 // 256-byte header (ticket counter, abort word) + one 16-byte status slot per tile.
-static size_t workspace_bytes_for(int64_t n) { return 256 + tiles_of(n) * sizeof(uint4); }
+static size_t workspace_bytes_for(int64_t n) { return 256 + status_slots(n) * sizeof(uint4); }
 
 static int carve(void* ws, size_t ws_bytes, int64_t n, Workspace& out) {
   if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return ASCAN_EWORKSPACE;
   if (ws_bytes < workspace_bytes_for(n)) return ASCAN_EWORKSPACE;
   char* base = static_cast<char*>(ws);
-  const size_t tiles = tiles_of(n);
-  (void)tiles;
+  const size_t tiles = status_slots(n);
   out.ticket = reinterpret_cast<uint32_t*>(base);
   out.st.abort = reinterpret_cast<uint32_t*>(base + 4);
   out.st.slots = reinterpret_cast<uint4*>(base + 256);
@@ -1110,10 +1118,6 @@ static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles,
   return 1;
 }
 
-// Tile order for a persistent launch.  Row mode needs rows that are whole
-// tiles (so the tile count -- and the workspace -- is that of the flat mode)
-// and at least two waves of rows, so that a tile's predecessor is old enough
-// to be read ahead.
 // Tile order of the TMA kernels: row mode needs row-aligned tiles (BL a
 // multiple of the tile) and pays off when sequences span several tiles: in
 // flat order their tiles are consecutive tickets of one wave, so every tile
@@ -1127,13 +1131,14 @@ static tma::TileSched make_sched(uint32_t num_tiles, int64_t N, int64_t BL, int6
   tma::TileSched sch{num_tiles, 0u, 0u, 0u, 1u};
   const int64_t C = BL > 0 ? N / BL : 0;
   const int mode = impl_mode();
-  const bool fits = BL % kTile == 0 && C >= 1 && C <= 0x7fffffffll;
-  const bool long_seqs = BL > S * static_cast<int64_t>(kTile);  // mean length above a tile
+  constexpr int64_t kT = tma::kTileElems;
+  const bool fits = BL % kT == 0 && C >= 1 && C <= 0x7fffffffll;
+  const bool long_seqs = BL > S * kT;  // mean length above a tile
   const bool row = mode == 4 ? fits : mode == 3 ? false : fits && long_seqs;
   if (row) {
     sch.row_mode = 1u;
     sch.rows = static_cast<uint32_t>(C);
-    sch.tiles_per_row = static_cast<uint32_t>(BL / kTile);
+    sch.tiles_per_row = static_cast<uint32_t>(BL / kT);
     sch.stride = static_cast<uint32_t>(C);
   }
   return sch;
@@ -1162,9 +1167,11 @@ static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, cudaStream_t s) {
   auto kern = io ? scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, true>
                  : scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false>;
   int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
-  tma::TileSched sch = make_sched(a.num_tiles, a.N, a.BL, a.S);
-  void* params[] = {&mg, &mx, &my, &mgo, const_cast<FwdArgs<T, IdxT>*>(&a), &n_tma_total, &sch};
-  return launch_cooperative(reinterpret_cast<const void*>(kern), smem, a.num_tiles, params, s);
+  FwdArgs<T, IdxT> b = a;
+  b.num_tiles = static_cast<uint32_t>(tma_tiles_of(a.N));
+  tma::TileSched sch = make_sched(b.num_tiles, b.N, b.BL, b.S);
+  void* params[] = {&mg, &mx, &my, &mgo, &b, &n_tma_total, &sch};
+  return launch_cooperative(reinterpret_cast<const void*>(kern), smem, b.num_tiles, params, s);
 }
 
 template <typename T, typename IdxT, bool CAUSAL>
@@ -1183,10 +1190,11 @@ static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, cudaStream_t s) {
   auto kern = io ? scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, true>
                  : scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false>;
   int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
-  tma::TileSched sch = make_sched(a.num_tiles, a.N, a.BL, a.S);
-  void* params[] = {&mdy, &mg, &mh, &mdx, &mdg, const_cast<BwdArgs<T, IdxT>*>(&a), &n_tma_total,
-                    &sch};
-  return launch_cooperative(reinterpret_cast<const void*>(kern), smem, a.num_tiles, params, s);
+  BwdArgs<T, IdxT> b = a;
+  b.num_tiles = static_cast<uint32_t>(tma_tiles_of(a.N));
+  tma::TileSched sch = make_sched(b.num_tiles, b.N, b.BL, b.S);
+  void* params[] = {&mdy, &mg, &mh, &mdx, &mdg, &b, &n_tma_total, &sch};
+  return launch_cooperative(reinterpret_cast<const void*>(kern), smem, b.num_tiles, params, s);
 }
 
 template <typename T, typename IdxT, int VEC>
@@ -1316,7 +1324,7 @@ static int check_common(const void* cu, int cu_type, int64_t S, int64_t C, int64
   if (dtype != ASCAN_F32 && dtype != ASCAN_F16 && dtype != ASCAN_BF16) return ASCAN_EINVAL;
   if (BL > 0 && C > INT64_MAX / BL) return ASCAN_EINVAL;
   // tile indices are 32-bit
-  if (tiles_of(C * BL) > 0xffffffffull) return ASCAN_EINVAL;
+  if (status_slots(C * BL) > 0xffffffffull) return ASCAN_EINVAL;
   return ASCAN_OK;
 }
 

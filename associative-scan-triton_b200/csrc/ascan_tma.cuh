@@ -1,12 +1,12 @@
 // ascan_tma.cuh -- persistent, TMA-fed scan kernels for sm_100a.
 //
-// One CTA per SM runs a loop over 4096-element tiles taken, in scan order,
-// from an atomic ticket counter.  Warp 8 is the producer: it takes the ticket,
+// Persistent CTAs (one per SM) run a loop over tiles of kTileElems elements
+// dealt to them in scan order.  The last warp is the producer: it takes the ticket,
 // waits for a free stage of a shared-memory ring, issues 2-D TMA loads of the
 // tile's inputs (tensor maps view the flat array as rows of 128 bytes, 128B
 // swizzle) and, while they fly, writes the tile's sequence-boundary bitmaps,
 // the neighbour scalars at the tile edges and the ragged tail of the array
-// into the stage's metadata.  Warps 0-7 consume: thread i owns elements
+// into the stage's metadata.  The other warps consume: thread i owns elements
 // [16i, 16i+16) of the tile (the swizzle makes those blocked reads
 // bank-conflict free), folds them serially, scans the per-thread aggregates
 // across the warp with shuffles and across warps through shared memory,
@@ -30,13 +30,24 @@
 namespace ascan {
 namespace tma {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;  // 256
+// CTA geometry: one CTA of 8 consumer warps per SM (4096-element tiles).
+// ASCAN_TMA_WARPS=4 at compile time builds two CTAs of 4 consumer warps per
+// SM (2048-element tiles) instead; measured on B200 it is within a few
+// percent at B=8, C=1536 (the SM still runs 8 consumer warps doing the same
+// work per element) and slower when rows are fewer than the CTAs.
+#ifndef ASCAN_TMA_WARPS
+#define ASCAN_TMA_WARPS 8
+#endif
+constexpr int kConsumerWarps = ASCAN_TMA_WARPS;
+constexpr int kCtasPerSm = 32 / kConsumerWarps / 4;       // 2 for 4 warps, 1 for 8
+static_assert(kCtasPerSm >= 1, "4 or 8 consumer warps");
+constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;        // + producer warp
 constexpr int kPerThread = 16;                   // elements per consumer thread
-constexpr int kTileElems = kConsumers * kPerThread;
-static_assert(kTileElems == kTile, "TMA and plain kernels share the tile size");
-constexpr int kBitWords = kTileElems / 32;       // 128
+constexpr int kTileElems = kConsumers * kPerThread;  // 4096 (8 warps) or 2048 (4 warps)
+static_assert(kTileElems <= kTile && kTile % kTileElems == 0,
+              "TMA tiles divide the plain kernels' tiles (status slots are sized for them)");
+constexpr int kBitWords = kTileElems / 32;
 constexpr int kCuCache = 1024;                   // cu_seqlens entries cached in smem
 constexpr uint32_t kDone = 0xffffffffu;
 
@@ -324,20 +335,14 @@ __device__ void build_meta(StageMeta<NIN, T>& m, const CuView<IdxT>& cu, int64_t
   int64_t nt = n_tma_total - p0;
   nt = nt < 0 ? 0 : (nt > n_valid ? n_valid : nt);
   // positions past the end of the array are isolated and never stored
-  uint32_t past[4] = {0u, 0u, 0u, 0u};
-  const uint32_t e0 = static_cast<uint32_t>(lane) * 128u;
-  if (n_valid < e0 + 128u) {
-    const uint32_t lo = n_valid > e0 ? n_valid - e0 : 0u;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint32_t a = lo > 32u * k ? lo - 32u * k : 0u;
-      if (a < 32u) past[k] = 0xffffffffu << a;
-    }
+  for (int w = lane; w < kBitWords; w += 32) {
+    const uint32_t e0 = static_cast<uint32_t>(w) * 32u;
+    const uint32_t past =
+        n_valid >= e0 + 32u ? 0u : (n_valid <= e0 ? 0xffffffffu : 0xffffffffu << (n_valid - e0));
+    m.sbits[w] = past;
+    m.ebits[w] = past;
+    m.obits[w] = 0u;
   }
-  const uint4 pv = make_uint4(past[0], past[1], past[2], past[3]);
-  *reinterpret_cast<uint4*>(&m.sbits[lane * 4]) = pv;
-  *reinterpret_cast<uint4*>(&m.ebits[lane * 4]) = pv;
-  *reinterpret_cast<uint4*>(&m.obits[lane * 4]) = make_uint4(0u, 0u, 0u, 0u);
   __syncwarp();
   const int64_t BL = cu.BL;
   int64_t t = t0;

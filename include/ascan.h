@@ -146,7 +146,7 @@ ASCAN_API int ascan_backward(const void* grad, const void* gates, const void* st
  * Arguments, results and other return codes are those of ascan_forward.
  */
 #define ASCAN_NOALLOC_SCRATCH_BYTES (2u << 20)
-#define ASCAN_NOALLOC_MAX_ELEMENTS 536805376ll /* 131056 tiles of 4096 elements */
+#define ASCAN_NOALLOC_MAX_ELEMENTS 536805376ll /* 131056 status slots of 4096 elements */
 ASCAN_API int ascan_forward_noalloc(const void* gates, const void* tokens, void* tokens_out,
                                     void* gates_out, const void* cu_seqlens, int cu_index_type,
                                     int64_t num_seq, int64_t num_channels, int64_t seq_total,

@@ -43,7 +43,7 @@ def test_workspace_size_grows_with_problem():
   small = lib.ascan_workspace_size(4, 128, 0)
   big = lib.ascan_workspace_size(1536, 8 * 65536, 0)
   assert small >= 256 and big > small
-  # 4096-element tiles: one 16-byte status slot per tile plus a 256-byte header
+  # one 16-byte status slot per 4096 elements plus a 256-byte header
   tiles = (1536 * 8 * 65536 + 4095) // 4096
   assert big == 256 + 16 * tiles
 

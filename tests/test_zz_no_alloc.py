@@ -82,4 +82,4 @@ def test_forward_noalloc_rejects_sizes_beyond_its_scratch():
           MAX_ELEMENTS + 1, 1, 0, 0, torch.cuda.current_stream().cuda_stream)
   assert rc == ASCAN_ETOOLARGE
   assert "fixed scratch" in _lib.strerror(rc)
-  assert np.int64(MAX_ELEMENTS) // 4096 == 131056  # whole 4096-element tiles
+  assert np.int64(MAX_ELEMENTS) // 4096 == 131056  # whole 4096-element status slots
