@@ -589,35 +589,50 @@ __device__ __forceinline__ void take_early(const uint4& raw, bool& te_known, Pfx
   }
 }
 
-// Slot hand-off in shared memory: value words, fence, then the tag.
+// Slot hand-off in shared memory: one 16-byte store of {a, b, flags, tag}.
 __device__ __forceinline__ void xs_put(float4* slot, const Pfx& p, uint32_t tag) {
-  volatile float* v = reinterpret_cast<volatile float*>(slot);
-  v[0] = p.a;
-  v[1] = p.b;
-  v[2] = __int_as_float(p.f);
-  __threadfence_block();
-  v[3] = __uint_as_float(tag);
+  asm volatile("st.volatile.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_addr(slot)),
+               "r"(__float_as_uint(p.a)), "r"(__float_as_uint(p.b)), "r"(static_cast<uint32_t>(p.f)),
+               "r"(tag)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 xs_load(const float4* slot) {
+  uint4 w;
+  asm volatile("ld.volatile.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+               : "r"(smem_addr(slot))
+               : "memory");
+  return w;
 }
 
 // Bounded wait of a whole warp for slot hand-offs: each lane with `need`
-// waits for its `slot` to carry `tag` and then reads it into `out` (other
-// lanes leave `out` alone).  Completion, timeout and the CTA's abort word are
-// decided by warp votes, so the result is the same in all lanes and the warp
-// never splits.  All lanes must call it.  false on timeout or abort.
+// waits for its `slot` to carry `tag` and then takes its value into `out`
+// (other lanes leave `out` alone).  The slot is written and read as one
+// 16-byte access, so a matching tag comes with its own value and no fence is
+// needed.  Completion, timeout and the CTA's abort word are decided by warp
+// votes, so the result is the same in all lanes and the warp never splits.
+// All lanes must call it.  false on timeout or abort.
 __device__ __forceinline__ bool xs_get_warp(const float4* slot, bool need, uint32_t tag,
                                             Pfx& out, const volatile int* abort_flag) {
-  const volatile float* v = reinterpret_cast<const volatile float*>(slot);
-  bool have = !need || __float_as_uint(v[3]) == tag;
+  uint4 w = make_uint4(0u, 0u, 0u, 0u);
+  bool have = !need;
+  if (need) {
+    w = xs_load(slot);
+    have = w.w == tag;
+  }
   if (!__all_sync(kFull, have)) {
     const unsigned long long t0 = globaltimer();
     while (true) {
-      if (!have) have = __float_as_uint(v[3]) == tag;
+      if (!have) {
+        w = xs_load(slot);
+        have = w.w == tag;
+      }
       if (__all_sync(kFull, have)) break;
       if (__any_sync(kFull, *abort_flag != 0 || wait_expired(t0))) return false;
     }
   }
-  __threadfence_block();
-  if (need) out = Pfx{v[0], v[1], __float_as_int(v[2])};
+  if (need) out = Pfx{__uint_as_float(w.x), __uint_as_float(w.y), static_cast<int>(w.z)};
   return true;
 }
 
