@@ -1096,20 +1096,51 @@ static int sm_count() {
 // caller falls back to the plain kernel), <0: error.
 static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles, void** params,
                               cudaStream_t s) {
+  // Per kernel and device: the shared-memory opt-in and the occupancy query
+  // run once (they are host-side driver calls, not free at small sizes).
+  struct Entry {
+    const void* kern;
+    int device;
+    int per_sm;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static int n_cache = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  int per_sm = -1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n_cache; ++i)
+      if (cache[i].kern == kern && cache[i].device == dev) per_sm = cache[i].per_sm;
+  }
+  if (per_sm < 0) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return ASCAN_ECUDA;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tma::kThreads, smem) !=
+        cudaSuccess)
+      return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (n_cache < 64) cache[n_cache++] = Entry{kern, dev, per_sm};
+  }
+  if (per_sm <= 0) return 0;
   const int sms = sm_count();
   if (sms <= 0) return 0;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem)) != cudaSuccess)
-    return ASCAN_ECUDA;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, tma::kThreads, smem) !=
-          cudaSuccess ||
-      per_sm <= 0)
-    return 0;
   const uint32_t resident = static_cast<uint32_t>(sms) * static_cast<uint32_t>(per_sm);
   const uint32_t grid = num_tiles < resident ? num_tiles : resident;
-  const cudaError_t e =
-      cudaLaunchCooperativeKernel(kern, dim3(grid), dim3(tma::kThreads), params, smem, s);
+  // cooperative through the launch attribute: also valid under stream capture
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(tma::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, kern, params);
   if (e != cudaSuccess) {
     fprintf(stderr, "ascan: cooperative launch failed: %s\n", cudaGetErrorString(e));
     cudaGetLastError();

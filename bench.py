@@ -347,6 +347,51 @@ def _time_shard_5b(dist, rank: int, world: int, device, steps: int = 10) -> dict
                       if world > 1 else "none (single GPU)"}
 
 
+def _small_t_graph(ast, device, reps: int = 200) -> dict:
+  """The launch-bound end of the sweep: B=8 sequences of T=128, C=1536 fp32,
+  one causal fwd+bwd step through the dispatcher API, called eagerly and
+  replayed from a CUDA graph captured once (same work, no host overhead)."""
+  from associative_scan_triton import _lib
+  Tn = 128
+  g, x, dy, cu = _make_workload(device, seed=7, T_=Tn)
+  y, dx, dg = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+  grid = (B, 1, C)
+
+  def step():
+    ast.forward_scan_full(g, x, cu, grid, REVERSE=False, CHUNK_SIZE=128, TESTING=False,
+                          tokens_out=y)
+    ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, grid, CHUNK_SIZE=128, CAUSAL=True)
+
+  def timed(fn):
+    for _ in range(10):
+      fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+      fn()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / reps
+
+  eager_ms = timed(step)
+  side = torch.cuda.Stream(device)
+  side.wait_stream(torch.cuda.current_stream(device))
+  with torch.cuda.stream(side):
+    step()
+  torch.cuda.current_stream(device).wait_stream(side)
+  graph = torch.cuda.CUDAGraph()
+  with torch.cuda.graph(graph):
+    step()
+  graph_ms = timed(graph.replay)
+  _lib.check_device_error(device)
+  del graph
+  n = g.numel()
+  return {"workload": "causal fwd+bwd, B=8 x T=128, C=1536, fp32", "eager_ms_per_step":
+          round(eager_ms, 4), "graph_ms_per_step": round(graph_ms, 4),
+          "graph_gbs": round(STEP_BYTES_PER_ELEM * n / (graph_ms * 1e-3) / 1e9, 1)}
+
+
 def _cpu_baseline(seconds: float = 10.0) -> dict:
   """The reference's CPU algorithm (fp64 sequential scan, oracle port) on a channel sample."""
   from oracle import oracle
@@ -494,6 +539,7 @@ def run_ours(args) -> dict | None:
     line["time_shard"] = time_shard
   if not args.no_sweep and world == 1:
     line["sweep_B8_C1536_fp32"] = _sweep(ast, device)
+    line["small_t_graph"] = _small_t_graph(ast, device)
   if not args.no_cpu_baseline and world == 1:
     line["cpu_baseline"] = _cpu_baseline(args.cpu_seconds)
   return line

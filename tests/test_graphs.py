@@ -1,0 +1,85 @@
+"""GPU: the dispatcher-level ops inside CUDA graphs.
+
+The launch-bound small-T regime (SURVEY's small-T overhead item; the
+reference loses to warpscan at T <= 256 on host overhead) is served by
+capturing the forward and backward calls once and replaying the graph: the
+workspace comes from the graph's memory pool, the status clear and the kernel
+launches are captured stream operations, and the persistent kernels'
+cooperative launch is a launch attribute, which graphs accept.  A replay with
+new inputs copied into the static buffers must match eager calls (bit for bit
+when no tile needs a look-back, whose carries may compose in another order).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import associative_scan_triton as ast
+from associative_scan_triton import _lib
+from scan_testlib import cu_of, make_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def _eager(g, x, dy, cu, S, C, reverse):
+  y = torch.empty_like(x)
+  ast.forward_scan_full(g, x, cu, (S, 1, C), REVERSE=reverse, CHUNK_SIZE=2, TESTING=False,
+                        tokens_out=y)
+  dx, dg = torch.empty_like(x), torch.empty_like(x)
+  ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, (S, 1, C), CHUNK_SIZE=2, CAUSAL=not reverse)
+  return y, dx, dg
+
+
+@pytest.mark.parametrize("impl", ["tma", "simple"])
+@pytest.mark.parametrize(("C", "seqlens", "reverse"), [
+  (1536, [128] * 8, False),          # the small-T headline shape
+  (64, [5000, 20000, 77], False),    # look-back across tiles
+  (300, [4096 * 3], True),           # row order, reverse
+])
+def test_graph_replay_matches_eager(impl, C, seqlens, reverse):
+  _lib.set_implementation(impl)
+  was = _lib.sync_check_enabled()
+  _lib.set_sync_check(False)  # no host synchronisation inside a capture
+  try:
+    S, BL = len(seqlens), sum(seqlens)
+    cu = cu_of(seqlens)
+    g, x = make_inputs(C, BL, gate="long", seed=1)
+    dy = torch.randn_like(x)
+    y, dx, dg = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+
+    def step():
+      ast.forward_scan_full(g, x, cu, (S, 1, C), REVERSE=reverse, CHUNK_SIZE=2, TESTING=False,
+                            tokens_out=y)
+      ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, (S, 1, C), CHUNK_SIZE=2,
+                                   CAUSAL=not reverse)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+      for _ in range(3):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+      step()
+    for seed in (2, 3):  # two replays with fresh inputs in the static buffers
+      g2, x2 = make_inputs(C, BL, gate="long", seed=seed)
+      dy2 = torch.randn(C, BL, generator=torch.Generator().manual_seed(seed)).cuda()
+      g.copy_(g2)
+      x.copy_(x2)
+      dy.copy_(dy2)
+      graph.replay()
+      torch.cuda.synchronize()
+      ye, dxe, dge = _eager(g2, x2, dy2, cu, S, C, reverse)
+      torch.cuda.synchronize()
+      if all(L <= 4096 and 4096 % L == 0 for L in seqlens):  # no look-back: same arithmetic
+        assert torch.equal(y, ye) and torch.equal(dx, dxe) and torch.equal(dg, dge)
+      else:  # look-back may compose the same carries in a different order
+        for got, want in ((y, ye), (dx, dxe), (dg, dge)):
+          torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-6)
+    _lib.check_device_error()
+    del graph
+  finally:
+    _lib.set_sync_check(was)
+    _lib.set_implementation("auto")
