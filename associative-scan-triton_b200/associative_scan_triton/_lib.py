@@ -49,6 +49,7 @@ EXPORTED_SYMBOLS = (
   "ascan_get_implementation",
   "ascan_get_device_error",
   "ascan_clear_device_error",
+  "ascan_selftest_waits",
 )
 
 IMPLEMENTATIONS = {"auto": 0, "simple": 1, "tma": 2, "tma-flat": 3, "tma-row": 4}
@@ -93,6 +94,9 @@ def _bind(lib) -> None:
                                          ctypes.POINTER(ctypes.c_longlong)]
   lib.ascan_clear_device_error.restype = ci
   lib.ascan_clear_device_error.argtypes = [ci]
+  lib.ascan_selftest_waits.restype = ci
+  lib.ascan_selftest_waits.argtypes = [p, sz, ctypes.c_longlong,
+                                       ctypes.POINTER(ctypes.c_longlong), p]
 
 
 def load(path: str | os.PathLike | None = None):

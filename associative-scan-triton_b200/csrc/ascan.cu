@@ -934,6 +934,44 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
 }
 
 // ---------------------------------------------------------------------------
+// Self-test of the bounded waits: three waits on conditions that nothing will
+// ever satisfy -- a stage barrier nobody arrives on, a hand-off slot nobody
+// tags, a look-back whose predecessor never publishes -- each of which must
+// give up after `limit_ns` and say so, leaving the context usable.
+// out[0]: barrier wait succeeded, out[1]: slot wait succeeded, out[2]:
+// look-back gave up, out[3]: elapsed nanoseconds of the three waits.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(32) selftest_waits_kernel(uint4* slots, uint32_t* abort_word,
+                                                           unsigned long long limit_ns,
+                                                           unsigned long long* out) {
+  __shared__ alignas(8) uint64_t bar;
+  __shared__ float4 slot;
+  __shared__ int cta_abort;
+  const int lane = threadIdx.x;
+  if (lane == 0) {
+    tma::mbar_init(&bar, 1);
+    slot = make_float4(0.f, 0.f, 0.f, __uint_as_float(tma::kNoTag));
+    cta_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  const unsigned long long t0 = globaltimer();
+  const bool got_bar = tma::mbar_wait_warp(&bar, 0u, limit_ns);  // phase 0 never completes
+  Pfx v = pfx_empty();
+  const bool got_slot = tma::xs_get_warp(&slot, true, 7u, v, &cta_abort, limit_ns);
+  bool timed_out = false;
+  (void)lookback_warp<kLookbackPerLane>(TileStatus{slots, abort_word}, 1u, lane, &timed_out, 1u,
+                                        limit_ns);
+  if (lane == 0) {
+    out[0] = got_bar ? 1ull : 0ull;
+    out[1] = got_slot ? 1ull : 0ull;
+    out[2] = timed_out ? 1ull : 0ull;
+    out[3] = globaltimer() - t0;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // shift_pad: out[t] = pad at boundaries, else data[t -/+ 1]
 // ---------------------------------------------------------------------------
 
@@ -1594,6 +1632,31 @@ int ascan_get_device_error(int device, unsigned int* code, long long* detail) {
   if (code) *code = c;
   if (detail) *detail = static_cast<long long>(d);
   return rc;
+}
+
+int ascan_selftest_waits(void* workspace, size_t workspace_bytes, long long limit_ns,
+                         long long* results, void* stream) {
+  if (!workspace || !results || workspace_bytes < 512 ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return ASCAN_EINVAL;
+  if (limit_ns < 1000000ll) limit_ns = 1000000ll;  // 1 ms .. the production limit
+  if (limit_ns > static_cast<long long>(kLookbackTimeoutNs))
+    limit_ns = static_cast<long long>(kLookbackTimeoutNs);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* base = static_cast<char*>(workspace);
+  auto* out = reinterpret_cast<unsigned long long*>(base);           // 4 words
+  auto* abort_word = reinterpret_cast<uint32_t*>(base + 64);
+  auto* slots = reinterpret_cast<uint4*>(base + 256);                // 16 slots
+  if (cudaMemsetAsync(workspace, 0, 512, s) != cudaSuccess) return ASCAN_ECUDA;
+  selftest_waits_kernel<<<1, 32, 0, s>>>(slots, abort_word,
+                                         static_cast<unsigned long long>(limit_ns), out);
+  if (cudaGetLastError() != cudaSuccess) return ASCAN_ECUDA;
+  unsigned long long host[4] = {0, 0, 0, 0};
+  if (cudaMemcpyAsync(host, out, sizeof(host), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return ASCAN_ECUDA;
+  for (int i = 0; i < 4; ++i) results[i] = static_cast<long long>(host[i]);
+  return ASCAN_OK;
 }
 
 int ascan_clear_device_error(int device) {

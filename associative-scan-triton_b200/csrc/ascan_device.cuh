@@ -365,11 +365,12 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   return t;
 }
 
-// True once more than kLookbackTimeoutNs have passed since t0.  The
-// difference is taken signed, so a timer reading that steps back never
-// counts as an expired wait.
-__device__ __forceinline__ bool wait_expired(unsigned long long t0) {
-  return static_cast<long long>(globaltimer() - t0) > static_cast<long long>(kLookbackTimeoutNs);
+// True once more than `limit_ns` (default kLookbackTimeoutNs) have passed
+// since t0.  The difference is taken signed, so a timer reading that steps
+// back never counts as an expired wait.
+__device__ __forceinline__ bool wait_expired(unsigned long long t0,
+                                             unsigned long long limit_ns = kLookbackTimeoutNs) {
+  return static_cast<long long>(globaltimer() - t0) > static_cast<long long>(limit_ns);
 }
 
 // Tile status records, one 16-byte slot per ticket: two 64-bit words
@@ -452,7 +453,8 @@ __device__ __forceinline__ uint32_t wait_status(const TileStatus& st, uint32_t t
 // was not published within the bounded wait (it then counts as empty).
 template <int K>
 __device__ __forceinline__ Pfx lookback_warp(const TileStatus& st, uint32_t ticket, int lane,
-                                             bool* timed_out, uint32_t stride = 1u) {
+                                             bool* timed_out, uint32_t stride = 1u,
+                                             unsigned long long limit_ns = kLookbackTimeoutNs) {
   Pfx te = pfx_empty();
   int64_t base = 0;  // distance (in predecessors) of this window's nearest slot, minus one
   bool lost = false;
@@ -492,7 +494,7 @@ __device__ __forceinline__ Pfx lookback_warp(const TileStatus& st, uint32_t tick
       if (poll == 0) t0 = globaltimer();
       __nanosleep(ns);
       if (ns < 256) ns <<= 1;
-      const bool give_up = launch_aborted(st) || wait_expired(t0);
+      const bool give_up = launch_aborted(st) || wait_expired(t0, limit_ns);
       if (__any_sync(kFull, give_up)) {
         if (lane == 0) set_aborted(st);
         lost = true;  // unpublished slots count as empty records

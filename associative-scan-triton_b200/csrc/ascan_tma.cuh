@@ -109,14 +109,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // lane polls (so every lane acquires), and both the completion and the
 // timeout are decided by warp votes, so all 32 lanes leave together with the
 // same result.  All lanes must call it.  false on timeout.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
+                                               unsigned long long limit_ns = kLookbackTimeoutNs) {
   bool done = mbar_try_wait(bar, parity);
   if (__all_sync(kFull, done)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
     if (!done) done = mbar_try_wait(bar, parity);
     if (__all_sync(kFull, done)) return true;
-    if (__any_sync(kFull, wait_expired(t0))) return false;
+    if (__any_sync(kFull, wait_expired(t0, limit_ns))) return false;
   }
 }
 
@@ -614,7 +615,8 @@ __device__ __forceinline__ uint4 xs_load(const float4* slot) {
 // votes, so the result is the same in all lanes and the warp never splits.
 // All lanes must call it.  false on timeout or abort.
 __device__ __forceinline__ bool xs_get_warp(const float4* slot, bool need, uint32_t tag,
-                                            Pfx& out, const volatile int* abort_flag) {
+                                            Pfx& out, const volatile int* abort_flag,
+                                            unsigned long long limit_ns = kLookbackTimeoutNs) {
   uint4 w = make_uint4(0u, 0u, 0u, 0u);
   bool have = !need;
   if (need) {
@@ -629,7 +631,7 @@ __device__ __forceinline__ bool xs_get_warp(const float4* slot, bool need, uint3
         have = w.w == tag;
       }
       if (__all_sync(kFull, have)) break;
-      if (__any_sync(kFull, *abort_flag != 0 || wait_expired(t0))) return false;
+      if (__any_sync(kFull, *abort_flag != 0 || wait_expired(t0, limit_ns))) return false;
     }
   }
   if (need) out = Pfx{__uint_as_float(w.x), __uint_as_float(w.y), static_cast<int>(w.z)};

@@ -244,6 +244,19 @@ ASCAN_API int ascan_get_implementation(void);
  */
 ASCAN_API int ascan_get_device_error(int device, unsigned int* code, long long* detail);
 
+/*
+ * Self-test of the kernels' bounded waits (no counterpart in the reference):
+ * one warp waits on a stage barrier nobody arrives on, on a hand-off slot
+ * nobody tags and on a look-back predecessor that never publishes, each with
+ * the limit `limit_ns` (clamped to 1 ms .. 2 s).  Every wait must give up and
+ * the context stay usable.  `workspace`: device memory of at least 512 bytes,
+ * 256-byte aligned (cleared here).  results[4] (host): barrier wait
+ * succeeded, slot wait succeeded, look-back gave up, elapsed nanoseconds.
+ * Synchronises `stream`.  Does not touch the sticky device error word.
+ */
+ASCAN_API int ascan_selftest_waits(void* workspace, size_t workspace_bytes, long long limit_ns,
+                                   long long* results, void* stream);
+
 /* Reset the sticky error word of `device`. */
 ASCAN_API int ascan_clear_device_error(int device);
 
