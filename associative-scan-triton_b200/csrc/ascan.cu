@@ -657,7 +657,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     // a, b hold the local prefixes: h = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV>(head);
     if (IO && lastmask != 0u) record_row_agg<REV>(a, b, lastmask, cm, P, p0 + o, BL, args.io.agg);
-    if (cm == 0xffffu) {
+    if (__all_sync(kFull, cm == 0xffffu)) {  // warp-uniform: no lane holds a head
 #pragma unroll
       for (int j = 0; j < kPerThread; ++j) {
         b[j] = fmaf(a[j], P.b, b[j]);
@@ -666,10 +666,9 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     } else {
 #pragma unroll
       for (int j = 0; j < kPerThread; ++j) {
-        if ((cm >> j) & 1u) {
-          b[j] = fmaf(a[j], P.b, b[j]);
-          if constexpr (GATES_OUT) a[j] *= P.a;
-        }
+        const bool c = (cm >> j) & 1u;
+        b[j] = c ? fmaf(a[j], P.b, b[j]) : b[j];
+        if constexpr (GATES_OUT) a[j] = c ? a[j] * P.a : a[j];
       }
     }
     const bool store = !IO || args.y != nullptr;  // false: aggregate-only pass

@@ -440,8 +440,10 @@ __device__ __forceinline__ Pfx fold16_inplace(float (&a)[kPerThread], float (&b)
                                               uint32_t head) {
   constexpr int j0 = REV ? kPerThread - 1 : 0;
   float A = a[j0], B = b[j0];
-  int f = kValid | static_cast<int>((head >> j0) & 1u);
-  if (head == 0u) {
+  const int f = kValid | (head != 0u ? kHead : 0);
+  // One path per warp (a warp vote, not a per-thread branch): a single lane
+  // holding a head must not make its whole warp run both loops.
+  if (__all_sync(kFull, head == 0u)) {
 #pragma unroll
     for (int jj = 1; jj < kPerThread; ++jj) {
       const int j = REV ? kPerThread - 1 - jj : jj;
@@ -454,14 +456,11 @@ __device__ __forceinline__ Pfx fold16_inplace(float (&a)[kPerThread], float (&b)
 #pragma unroll
     for (int jj = 1; jj < kPerThread; ++jj) {
       const int j = REV ? kPerThread - 1 - jj : jj;
-      if ((head >> j) & 1u) {
-        A = a[j];
-        B = b[j];
-        f |= kHead;
-      } else {
-        B = fmaf(a[j], B, b[j]);
-        A *= a[j];
-      }
+      const bool h = (head >> j) & 1u;  // a head restarts the recurrence (selects, no branch)
+      const float Bn = fmaf(a[j], B, b[j]);
+      const float An = A * a[j];
+      B = h ? b[j] : Bn;
+      A = h ? a[j] : An;
       a[j] = A;
       b[j] = B;
     }
