@@ -416,14 +416,14 @@ namespace ascan {
 // CTAs, 1 KB of each reserved by the hardware.
 constexpr size_t kSmemBudget = (228 * 1024) / tma::kCtasPerSm - 1024;
 
-template <typename T, int NIN, int NOUT, int NS = 6>
+template <typename T, int NIN, int NOUT, bool RG = false, int NS = 6>
 constexpr int ring_depth() {
   if constexpr (NS <= 2)
     return 2;
-  else if constexpr (tma::smem_bytes<NIN, NOUT, NS, T>() <= kSmemBudget)
+  else if constexpr (tma::smem_bytes<NIN, NOUT, NS, T, RG>() <= kSmemBudget)
     return NS;
   else
-    return ring_depth<T, NIN, NOUT, NS - 1>();
+    return ring_depth<T, NIN, NOUT, RG, NS - 1>();
 }
 
 // Producer warp of both kernels: TMA loads and per-tile metadata.  Tickets
@@ -436,8 +436,10 @@ constexpr int ring_depth() {
 // the carry-in there instead of polling global memory, and the producer never
 // waits for that read.
 // `Extra` fills the halo scalars and the ragged tail of one stage.
-template <typename T, typename IdxT, bool REV, int NIN, int NOUT, int NS, typename Extra>
-__device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
+// RG (ragged rows): tiles start anywhere inside a 128-byte TMA row; the box is
+// one TMA row taller and the tile's offset into it travels in the metadata.
+template <typename T, typename IdxT, bool REV, int NIN, int NOUT, int NS, bool RG, typename Extra>
+__device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, RG>& sm,
                                              const CUtensorMap* const* maps,
                                              const tma::CuView<IdxT>& cu, int64_t N,
                                              int64_t n_tma_total, const tma::TileSched& sch,
@@ -509,12 +511,15 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
       limit = N;
     }
     const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow);
+    constexpr uint32_t kBoxBytes = (Fmt<T>::kRows + (RG ? 1 : 0)) * 128u;
     const bool read_pred = sch.row_mode && ticket >= sch.stride;
     if (lane == 0) {
       m.ticket = ticket;
+      if constexpr (RG)
+        m.shift = static_cast<uint32_t>(p0 - static_cast<int64_t>(row) * Fmt<T>::kElemsPerRow);
       if (!read_pred) m.te_raw[1] = m.te_raw[3] = kStatusNone;
       // the first n_load inputs (an aggregate-only backward skips the states)
-      mbar_expect_tx(&sm.full[stage], n_load * Fmt<T>::kBytes + (read_pred ? 16u : 0u));
+      mbar_expect_tx(&sm.full[stage], n_load * kBoxBytes + (read_pred ? 16u : 0u));
       for (int k = 0; k < n_load; ++k) tma_load_2d(sm.in[stage][k], maps[k], 0, row, &sm.full[stage]);
       if (read_pred) bulk_load(m.te_raw, st.slots + (ticket - sch.stride), 16u, &sm.full[stage]);
     }
@@ -552,7 +557,7 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T>& sm,
 
 // IO: the launch serves a time slab (RowIO in use or no outputs); compiled
 // separately so the ordinary kernels carry none of that code.
-template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO>
+template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO, bool RG>
 __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     scan_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_g,
                         const __grid_constant__ CUtensorMap map_x,
@@ -561,7 +566,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
                         int64_t n_tma_total, const tma::TileSched sch) {
   using namespace tma;
   constexpr int NIN = 2, NOUT = GATES_OUT ? 2 : 1;
-  using Sm = Smem<NIN, NOUT, NS, T>;
+  using Sm = Smem<NIN, NOUT, NS, T, RG>;
   Sm& sm = smem_view<Sm>();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t S = args.S, BL = args.BL, N = args.N;
@@ -586,7 +591,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
 
   if (warp == kConsumerWarps) {
     const CUtensorMap* maps[NIN] = {&map_g, &map_x};
-    run_producer<T, IdxT, REV, NIN, NOUT, NS>(
+    run_producer<T, IdxT, REV, NIN, NOUT, NS, RG>(
         sm, maps, cu, N, n_tma_total, sch, args.st, lane,
         [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
             uint64_t*) {
@@ -622,8 +627,14 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
     const bool has_outside = m.has_outside != 0u;
     float a[kPerThread], b[kPerThread];
-    read_block<T, NIN>(sm.in[stage][0], tc, m, 0, o, n_tma, n_valid, 1.f, a);
-    read_block<T, NIN>(sm.in[stage][1], tc, m, 1, o, n_tma, n_valid, 0.f, b);
+    if constexpr (RG) {
+      const uint32_t shift = m.shift;
+      read_block_shifted<T, NIN>(sm.in[stage][0], m, 0, o, shift, n_tma, n_valid, 1.f, a);
+      read_block_shifted<T, NIN>(sm.in[stage][1], m, 1, o, shift, n_tma, n_valid, 0.f, b);
+    } else {
+      read_block<T, NIN>(sm.in[stage][0], tc, m, 0, o, n_tma, n_valid, 1.f, a);
+      read_block<T, NIN>(sm.in[stage][1], tc, m, 1, o, n_tma, n_valid, 0.f, b);
+    }
     const uint32_t head =
         ((REV ? m.ebits[bit_word] : m.sbits[bit_word]) >> bit_shift) & 0xffffu;
     const uint32_t omask = has_outside ? (m.obits[bit_word] >> bit_shift) & 0xffffu : 0u;
@@ -679,7 +690,16 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     // this warp's slice goes out by TMA when it lies wholly inside the tile's
     // TMA-covered part (never past a row end or the array end)
     const bool slice_tma =
-        store && !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
+        !RG && store && !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
+    if constexpr (RG) {
+      if (__all_sync(kFull, direct == 0xffffu)) {
+        // ragged rows: a wholly valid warp slice leaves by realigned 16-byte stores
+        const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T>::kVec);
+        store_realigned<T>(args.y, p0 + o, r, b, lane);
+        if constexpr (GATES_OUT) store_realigned<T>(args.gout, p0 + o, r, a, lane);
+        direct = 0u;
+      }
+    }
     if (slice_tma) {
       write_block<T>(sm.out[obuf][0], tc, b);
       if constexpr (GATES_OUT) write_block<T>(sm.out[obuf][1], tc, a);
@@ -710,7 +730,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
   if (lane == 0) bulk_wait_all();
 }
 
-template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO>
+template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO, bool RG>
 __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     scan_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dy,
                         const __grid_constant__ CUtensorMap map_g,
@@ -721,7 +741,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
   using namespace tma;
   constexpr bool REV = CAUSAL;
   constexpr int NIN = 3, NOUT = 2;
-  using Sm = Smem<NIN, NOUT, NS, T>;
+  using Sm = Smem<NIN, NOUT, NS, T, RG>;
   Sm& sm = smem_view<Sm>();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t S = args.S, BL = args.BL, N = args.N;
@@ -746,7 +766,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
 
   if (warp == kConsumerWarps) {
     const CUtensorMap* maps[NIN] = {&map_dy, &map_g, &map_h};
-    run_producer<T, IdxT, REV, NIN, NOUT, NS>(
+    run_producer<T, IdxT, REV, NIN, NOUT, NS, RG>(
         sm, maps, cu, N, n_tma_total, sch, args.st, lane,
         [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
             uint64_t* bar) {
@@ -762,26 +782,37 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
             // starts are 16-byte aligned, and so are the blocks [pn, pn+V) and
             // [p0-V, p0).  A next block that would reach past the array end
             // is read directly (the array's last tile only).
+            // Ragged rows (RG): tiles start anywhere, so the copies fetch the
+            // aligned 16-byte blocks holding the neighbours, and the index of
+            // the neighbour inside its block travels in the metadata.
             constexpr int V = 16 / static_cast<int>(sizeof(T));
             const int64_t pn = p0 + kTileElems;
             const int kn = CAUSAL ? 0 : 1, kp = CAUSAL ? 1 : 0;  // halo slots
             const T* const arr[2] = {args.g, args.h};
             const float ident[2] = {1.f, 0.f};
             uint32_t bulk = 0u;
-            if (pn + V <= N) {
+            int64_t bn = pn, bp = p0 - V;  // the two blocks' first elements
+            if constexpr (RG) {
+              bn = pn - pn % V;
+              bp = p0 > 0 ? (p0 - 1) - (p0 - 1) % V : 0;
+            }
+            if (bn + V <= N) {
               bulk |= 1u << kn;
+              if constexpr (RG) m.halo_idx[kn] = static_cast<uint32_t>(pn - bn);
             } else {
               m.halo[kn] = pn < N ? Cvt<T>::to(arr[kn][pn]) : ident[kn];
             }
-            if (p0 >= V) {
+            // never a block that reaches past the array end
+            if (RG ? (p0 > 0 && bp + V <= N) : p0 >= V) {
               bulk |= 1u << kp;
+              if constexpr (RG) m.halo_idx[kp] = static_cast<uint32_t>(p0 - 1 - bp);
             } else {
               m.halo[kp] = p0 > 0 ? Cvt<T>::to(arr[kp][p0 - 1]) : ident[kp];
             }
             m.halo_bulk = bulk;
             if (bulk) mbar_expect_tx(bar, 16u * static_cast<uint32_t>(__popc(bulk)));
-            if (bulk & (1u << kn)) bulk_load(m.halo_raw[kn], arr[kn] + pn, 16u, bar);
-            if (bulk & (1u << kp)) bulk_load(m.halo_raw[kp], arr[kp] + (p0 - V), 16u, bar);
+            if (bulk & (1u << kn)) bulk_load(m.halo_raw[kn], arr[kn] + bn, 16u, bar);
+            if (bulk & (1u << kp)) bulk_load(m.halo_raw[kp], arr[kp] + bp, 16u, bar);
           }
         },
         IO && args.dx == nullptr ? 2 : NIN);  // aggregate-only: the states are never read
@@ -812,27 +843,41 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
     const bool has_outside = m.has_outside != 0u;
     float dyv[kPerThread], gv[kPerThread], hv[kPerThread];
-    read_block<T, NIN>(sm.in[stage][0], tc, m, 0, o, n_tma, n_valid, 0.f, dyv);
-    read_block<T, NIN>(sm.in[stage][1], tc, m, 1, o, n_tma, n_valid, 1.f, gv);
-    read_block<T, NIN>(sm.in[stage][2], tc, m, 2, o, n_tma, n_valid, 0.f, hv);
+    // ragged rows: the tile sits `shift` elements into its buffers
+    const uint32_t shift = RG ? m.shift : 0u;
+    if constexpr (RG) {
+      read_block_shifted<T, NIN>(sm.in[stage][0], m, 0, o, shift, n_tma, n_valid, 0.f, dyv);
+      read_block_shifted<T, NIN>(sm.in[stage][1], m, 1, o, shift, n_tma, n_valid, 1.f, gv);
+      read_block_shifted<T, NIN>(sm.in[stage][2], m, 2, o, shift, n_tma, n_valid, 0.f, hv);
+    } else {
+      read_block<T, NIN>(sm.in[stage][0], tc, m, 0, o, n_tma, n_valid, 0.f, dyv);
+      read_block<T, NIN>(sm.in[stage][1], tc, m, 1, o, n_tma, n_valid, 1.f, gv);
+      read_block<T, NIN>(sm.in[stage][2], tc, m, 2, o, n_tma, n_valid, 0.f, hv);
+    }
     // neighbours across the thread boundary: from the tile, or the tile-edge halo
     constexpr int V = 16 / static_cast<int>(sizeof(T));
-    const float halo_g = (m.halo_bulk & 1u) ? Cvt<T>::to(m.halo_raw[0][CAUSAL ? 0 : V - 1])
-                                            : m.halo[0];
-    const float halo_h = (m.halo_bulk & 2u) ? Cvt<T>::to(m.halo_raw[1][CAUSAL ? V - 1 : 0])
-                                            : m.halo[1];
+    float halo_g, halo_h;
+    if constexpr (RG) {
+      halo_g = (m.halo_bulk & 1u) ? Cvt<T>::to(m.halo_raw[0][m.halo_idx[0]]) : m.halo[0];
+      halo_h = (m.halo_bulk & 2u) ? Cvt<T>::to(m.halo_raw[1][m.halo_idx[1]]) : m.halo[1];
+    } else {  // aligned tiles: the neighbours sit at fixed places of their blocks
+      halo_g = (m.halo_bulk & 1u) ? Cvt<T>::to(m.halo_raw[0][CAUSAL ? 0 : V - 1]) : m.halo[0];
+      halo_h = (m.halo_bulk & 2u) ? Cvt<T>::to(m.halo_raw[1][CAUSAL ? V - 1 : 0]) : m.halo[1];
+    }
     float g_nb, h_nb;
     if (CAUSAL) {
       g_nb = (o + kPerThread < static_cast<uint32_t>(kTileElems))
-                 ? tile_elem<T, NIN>(sm.in[stage][1], m, 1, o + kPerThread, n_tma, n_valid, 1.f)
+                 ? tile_elem<T, NIN>(sm.in[stage][1], m, 1, o + kPerThread, n_tma, n_valid, 1.f,
+                                     shift)
                  : halo_g;
-      h_nb = (o > 0) ? tile_elem<T, NIN>(sm.in[stage][2], m, 2, o - 1, n_tma, n_valid, 0.f)
+      h_nb = (o > 0) ? tile_elem<T, NIN>(sm.in[stage][2], m, 2, o - 1, n_tma, n_valid, 0.f, shift)
                      : halo_h;
     } else {
-      g_nb = (o > 0) ? tile_elem<T, NIN>(sm.in[stage][1], m, 1, o - 1, n_tma, n_valid, 1.f)
+      g_nb = (o > 0) ? tile_elem<T, NIN>(sm.in[stage][1], m, 1, o - 1, n_tma, n_valid, 1.f, shift)
                      : halo_g;
       h_nb = (o + kPerThread < static_cast<uint32_t>(kTileElems))
-                 ? tile_elem<T, NIN>(sm.in[stage][2], m, 2, o + kPerThread, n_tma, n_valid, 0.f)
+                 ? tile_elem<T, NIN>(sm.in[stage][2], m, 2, o + kPerThread, n_tma, n_valid, 0.f,
+                                     shift)
                  : halo_h;
     }
     const uint32_t smask = (m.sbits[bit_word] >> bit_shift) & 0xffffu;
@@ -901,7 +946,16 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     // this warp's slice goes out by TMA when it lies wholly inside the tile's
     // TMA-covered part (never past a row end or the array end)
     const bool slice_tma =
-        store && !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
+        !RG && store && !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
+    if constexpr (RG) {
+      if (__all_sync(kFull, direct == 0xffffu)) {
+        // ragged rows: a wholly valid warp slice leaves by realigned 16-byte stores
+        const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T>::kVec);
+        store_realigned<T>(args.dx, p0 + o, r, dyv, lane);
+        store_realigned<T>(args.dg, p0 + o, r, gv, lane);
+        direct = 0u;
+      }
+    }
     if (slice_tma) {
       write_block<T>(sm.out[obuf][0], tc, dyv);
       write_block<T>(sm.out[obuf][1], tc, gv);
@@ -1020,9 +1074,8 @@ struct Workspace {
   uint32_t* ticket;
   TileStatus st;
   size_t clear_bytes;
+  bool allow_ragged;  // room for the status slots of ragged row order
 };
-
-static size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 // Tiles of the plain kernels (kTile elements) and of the persistent TMA
 // kernels (tma::kTileElems, a divisor of kTile); status slots are counted in
@@ -1031,16 +1084,29 @@ static size_t tiles_of(int64_t n) { return static_cast<size_t>((n + kTile - 1) /
 static size_t tma_tiles_of(int64_t n) {
   return static_cast<size_t>((n + tma::kTileElems - 1) / tma::kTileElems);
 }
-static size_t status_slots(int64_t n) { return tma_tiles_of(n); }
+// Row order with ragged rows (BL not a multiple of the tile) cuts every row
+// into ceil(BL / tile) tiles, a few more than the flat count.
+static size_t status_slots(int64_t C, int64_t BL, bool ragged) {
+  const size_t flat = tma_tiles_of(C * BL);
+  if (!ragged || BL < tma::kTileElems) return flat;  // ragged rows are at least a tile
+  const size_t rows = static_cast<size_t>(C) *
+                      static_cast<size_t>((BL + tma::kTileElems - 1) / tma::kTileElems);
+  return rows > flat ? rows : flat;
+}
 
 // 256-byte header (ticket counter, abort word) + one 16-byte status slot per tile.
-static size_t workspace_bytes_for(int64_t n) { return 256 + status_slots(n) * sizeof(uint4); }
+static size_t workspace_bytes_for(int64_t C, int64_t BL, bool ragged) {
+  return 256 + status_slots(C, BL, ragged) * sizeof(uint4);
+}
 
-static int carve(void* ws, size_t ws_bytes, int64_t n, Workspace& out) {
+// A workspace of the flat size is accepted; ragged row order is then simply
+// not used (the flat order needs fewer status slots).
+static int carve(void* ws, size_t ws_bytes, int64_t C, int64_t BL, Workspace& out) {
   if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return ASCAN_EWORKSPACE;
-  if (ws_bytes < workspace_bytes_for(n)) return ASCAN_EWORKSPACE;
+  if (ws_bytes < workspace_bytes_for(C, BL, false)) return ASCAN_EWORKSPACE;
   char* base = static_cast<char*>(ws);
-  const size_t tiles = status_slots(n);
+  out.allow_ragged = ws_bytes >= workspace_bytes_for(C, BL, true);
+  const size_t tiles = status_slots(C, BL, out.allow_ragged);
   out.ticket = reinterpret_cast<uint32_t*>(base);
   out.st.abort = reinterpret_cast<uint32_t*>(base + 4);
   out.st.slots = reinterpret_cast<uint4*>(base + 256);
@@ -1195,35 +1261,46 @@ static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles,
 // the flat order is slightly faster (a wave reads one contiguous range).
 // Implementations 3 and 4 force the flat and the row order; both orders give
 // the same results up to floating-point reassociation.
-static tma::TileSched make_sched(uint32_t num_tiles, int64_t N, int64_t BL, int64_t S) {
-  tma::TileSched sch{num_tiles, 0u, 0u, 0u, 1u};
+// allow_ragged: rows that are not whole tiles may be cut into whole tiles and
+// a partial last one (the workspace has their status slots and the launch
+// has no slab I/O).
+static tma::TileSched make_sched(uint32_t num_tiles, int64_t N, int64_t BL, int64_t S,
+                                 bool allow_ragged) {
+  tma::TileSched sch{num_tiles, 0u, 0u, 0u, 1u, 0u};
   const int64_t C = BL > 0 ? N / BL : 0;
   const int mode = impl_mode();
   constexpr int64_t kT = tma::kTileElems;
-  const bool fits = BL % kT == 0 && C >= 1 && C <= 0x7fffffffll;
+  const int64_t per_row = BL > 0 ? (BL + kT - 1) / kT : 0;
+  const bool aligned = BL % kT == 0;
+  const bool fits = BL >= kT && C >= 1 && C <= 0x7fffffffll && C * per_row <= 0xffffffffll &&
+                    (aligned || allow_ragged);
   const bool long_seqs = BL > S * kT;  // mean length above a tile
   const bool row = mode == 4 ? fits : mode == 3 ? false : fits && long_seqs;
   if (row) {
     sch.row_mode = 1u;
     sch.rows = static_cast<uint32_t>(C);
-    sch.tiles_per_row = static_cast<uint32_t>(BL / kT);
+    sch.tiles_per_row = static_cast<uint32_t>(per_row);
     sch.stride = static_cast<uint32_t>(C);
+    sch.ragged = aligned ? 0u : 1u;
+    sch.num_tiles = static_cast<uint32_t>(C * per_row);
   }
   return sch;
 }
 
 // 1: launched, 0: not applicable (caller falls back to the plain kernel), <0: error
-template <typename T, typename IdxT, bool REV, bool GOUT>
-static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, cudaStream_t s) {
+template <typename T, typename IdxT, bool REV, bool GOUT, bool RG>
+static int launch_fwd_tma_sched(const FwdArgs<T, IdxT>& a, const tma::TileSched& sch0, bool io,
+                                cudaStream_t s) {
   constexpr int NOUT = GOUT ? 2 : 1;
-  constexpr int NS = ring_depth<T, 2, NOUT>();
-  constexpr size_t smem = tma::smem_bytes<2, NOUT, NS, T>();
+  constexpr int NS = ring_depth<T, 2, NOUT, RG>();
+  constexpr size_t smem = tma::smem_bytes<2, NOUT, NS, T, RG>();
   static_assert(smem <= kSmemBudget, "TMA forward ring does not fit in shared memory");
   const int64_t rows = a.N / tma::Fmt<T>::kElemsPerRow;
   CUtensorMap mg, mx, my, mgo;
   constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;  // stores: one warp's slice
+  constexpr int kInRows = tma::Fmt<T>::kRows + (RG ? 1 : 0);     // ragged: one more row
   // an aggregate-only pass stores nothing: its output map is a never-used view of g
-  if (!make_map<T>(&mg, a.g, rows) || !make_map<T>(&mx, a.x, rows) ||
+  if (!make_map<T>(&mg, a.g, rows, kInRows) || !make_map<T>(&mx, a.x, rows, kInRows) ||
       !make_map<T>(&my, a.y ? a.y : a.g, rows, kPart))
     return 0;
   if (GOUT) {
@@ -1231,38 +1308,68 @@ static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, cudaStream_t s) {
   } else {
     mgo = my;
   }
-  const bool io = a.io.carry || a.io.halo || a.io.agg || !a.y;
-  auto kern = io ? scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, true>
-                 : scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false>;
+  const void* kern;
+  if constexpr (RG)
+    kern = reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false, true>);
+  else
+    kern = io ? reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, true, false>)
+              : reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false, false>);
   int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
   FwdArgs<T, IdxT> b = a;
-  b.num_tiles = static_cast<uint32_t>(tma_tiles_of(a.N));
-  tma::TileSched sch = make_sched(b.num_tiles, b.N, b.BL, b.S);
+  tma::TileSched sch = sch0;
+  b.num_tiles = sch.num_tiles;
   void* params[] = {&mg, &mx, &my, &mgo, &b, &n_tma_total, &sch};
-  return launch_cooperative(reinterpret_cast<const void*>(kern), smem, b.num_tiles, params, s);
+  return launch_cooperative(kern, smem, b.num_tiles, params, s);
 }
 
-template <typename T, typename IdxT, bool CAUSAL>
-static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, cudaStream_t s) {
-  constexpr int NS = ring_depth<T, 3, 2>();
-  constexpr size_t smem = tma::smem_bytes<3, 2, NS, T>();
+// allow_ragged is passed beside the kernel arguments, not inside them: the
+// argument structs are what the kernels receive.
+template <typename T, typename IdxT, bool REV, bool GOUT>
+static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, bool allow_ragged, cudaStream_t s) {
+  const bool io = a.io.carry || a.io.halo || a.io.agg || !a.y;
+  // ragged rows need the shifted-tile kernels, which exist without slab I/O only
+  const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(a.N)), a.N, a.BL,
+                                        a.S, allow_ragged && !io);
+  if (sch.ragged) return launch_fwd_tma_sched<T, IdxT, REV, GOUT, true>(a, sch, io, s);
+  return launch_fwd_tma_sched<T, IdxT, REV, GOUT, false>(a, sch, io, s);
+}
+
+template <typename T, typename IdxT, bool CAUSAL, bool RG>
+static int launch_bwd_tma_sched(const BwdArgs<T, IdxT>& a, const tma::TileSched& sch0, bool io,
+                                cudaStream_t s) {
+  constexpr int NS = ring_depth<T, 3, 2, RG>();
+  constexpr size_t smem = tma::smem_bytes<3, 2, NS, T, RG>();
   static_assert(smem <= kSmemBudget, "TMA backward ring does not fit in shared memory");
   const int64_t rows = a.N / tma::Fmt<T>::kElemsPerRow;
   CUtensorMap mdy, mg, mh, mdx, mdg;
   constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;  // stores: one warp's slice
-  if (!make_map<T>(&mdy, a.dy, rows) || !make_map<T>(&mg, a.g, rows) ||
-      !make_map<T>(&mh, a.h, rows) || !make_map<T>(&mdx, a.dx ? a.dx : a.dy, rows, kPart) ||
+  constexpr int kInRows = tma::Fmt<T>::kRows + (RG ? 1 : 0);     // ragged: one more row
+  if (!make_map<T>(&mdy, a.dy, rows, kInRows) || !make_map<T>(&mg, a.g, rows, kInRows) ||
+      !make_map<T>(&mh, a.h, rows, kInRows) ||
+      !make_map<T>(&mdx, a.dx ? a.dx : a.dy, rows, kPart) ||
       !make_map<T>(&mdg, a.dg ? a.dg : a.dy, rows, kPart))
     return 0;
-  const bool io = a.io.carry || a.io.halo || a.io.agg || !a.dx;
-  auto kern = io ? scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, true>
-                 : scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false>;
+  const void* kern;
+  if constexpr (RG)
+    kern = reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false, true>);
+  else
+    kern = io ? reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, true, false>)
+              : reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false, false>);
   int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
   BwdArgs<T, IdxT> b = a;
-  b.num_tiles = static_cast<uint32_t>(tma_tiles_of(a.N));
-  tma::TileSched sch = make_sched(b.num_tiles, b.N, b.BL, b.S);
+  tma::TileSched sch = sch0;
+  b.num_tiles = sch.num_tiles;
   void* params[] = {&mdy, &mg, &mh, &mdx, &mdg, &b, &n_tma_total, &sch};
-  return launch_cooperative(reinterpret_cast<const void*>(kern), smem, b.num_tiles, params, s);
+  return launch_cooperative(kern, smem, b.num_tiles, params, s);
+}
+
+template <typename T, typename IdxT, bool CAUSAL>
+static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, bool allow_ragged, cudaStream_t s) {
+  const bool io = a.io.carry || a.io.halo || a.io.agg || !a.dx;
+  const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(a.N)), a.N, a.BL,
+                                        a.S, allow_ragged && !io);
+  if (sch.ragged) return launch_bwd_tma_sched<T, IdxT, CAUSAL, true>(a, sch, io, s);
+  return launch_bwd_tma_sched<T, IdxT, CAUSAL, false>(a, sch, io, s);
 }
 
 template <typename T, typename IdxT, int VEC>
@@ -1306,17 +1413,17 @@ static int fwd_typed(const void* g, const void* x, void* y, void* gout, const vo
     if (!vec || a.N < tma::Fmt<T>::kElemsPerRow) return ASCAN_EINVAL;
     int rc;
     if (reverse)
-      rc = gout ? launch_fwd_tma<T, IdxT, true, true>(a, s) : launch_fwd_tma<T, IdxT, true, false>(a, s);
+      rc = gout ? launch_fwd_tma<T, IdxT, true, true>(a, w.allow_ragged, s) : launch_fwd_tma<T, IdxT, true, false>(a, w.allow_ragged, s);
     else
-      rc = gout ? launch_fwd_tma<T, IdxT, false, true>(a, s) : launch_fwd_tma<T, IdxT, false, false>(a, s);
+      rc = gout ? launch_fwd_tma<T, IdxT, false, true>(a, w.allow_ragged, s) : launch_fwd_tma<T, IdxT, false, false>(a, w.allow_ragged, s);
     return rc > 0 ? ASCAN_OK : (rc == 0 ? ASCAN_EINVAL : rc);
   }
   if (vec && use_tma() && a.N >= tma::Fmt<T>::kElemsPerRow) {
     int rc;
     if (reverse)
-      rc = gout ? launch_fwd_tma<T, IdxT, true, true>(a, s) : launch_fwd_tma<T, IdxT, true, false>(a, s);
+      rc = gout ? launch_fwd_tma<T, IdxT, true, true>(a, w.allow_ragged, s) : launch_fwd_tma<T, IdxT, true, false>(a, w.allow_ragged, s);
     else
-      rc = gout ? launch_fwd_tma<T, IdxT, false, true>(a, s) : launch_fwd_tma<T, IdxT, false, false>(a, s);
+      rc = gout ? launch_fwd_tma<T, IdxT, false, true>(a, w.allow_ragged, s) : launch_fwd_tma<T, IdxT, false, false>(a, w.allow_ragged, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
   }
   if (vec)
@@ -1360,11 +1467,11 @@ static int bwd_typed(const void* dy, const void* g, const void* h, void* dx, voi
   const bool slab = io.carry || io.halo || io.agg || !dx;
   if (slab) {
     if (!vec || a.N < tma::Fmt<T>::kElemsPerRow) return ASCAN_EINVAL;
-    const int rc = causal ? launch_bwd_tma<T, IdxT, true>(a, s) : launch_bwd_tma<T, IdxT, false>(a, s);
+    const int rc = causal ? launch_bwd_tma<T, IdxT, true>(a, w.allow_ragged, s) : launch_bwd_tma<T, IdxT, false>(a, w.allow_ragged, s);
     return rc > 0 ? ASCAN_OK : (rc == 0 ? ASCAN_EINVAL : rc);
   }
   if (vec && use_tma() && a.N >= tma::Fmt<T>::kElemsPerRow) {
-    const int rc = causal ? launch_bwd_tma<T, IdxT, true>(a, s) : launch_bwd_tma<T, IdxT, false>(a, s);
+    const int rc = causal ? launch_bwd_tma<T, IdxT, true>(a, w.allow_ragged, s) : launch_bwd_tma<T, IdxT, false>(a, w.allow_ragged, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
   }
   if (vec)
@@ -1392,7 +1499,7 @@ static int check_common(const void* cu, int cu_type, int64_t S, int64_t C, int64
   if (dtype != ASCAN_F32 && dtype != ASCAN_F16 && dtype != ASCAN_BF16) return ASCAN_EINVAL;
   if (BL > 0 && C > INT64_MAX / BL) return ASCAN_EINVAL;
   // tile indices are 32-bit
-  if (status_slots(C * BL) > 0xffffffffull) return ASCAN_EINVAL;
+  if (status_slots(C, BL, false) > 0xffffffffull) return ASCAN_EINVAL;
   return ASCAN_OK;
 }
 
@@ -1427,7 +1534,7 @@ const char* ascan_strerror(int status) {
 size_t ascan_workspace_size(int64_t num_channels, int64_t seq_total, int dtype) {
   (void)dtype;
   if (num_channels <= 0 || seq_total <= 0) return 256;
-  return workspace_bytes_for(num_channels * seq_total);
+  return workspace_bytes_for(num_channels, seq_total, true);
 }
 
 #define ASCAN_DISPATCH_TYPES(DTYPE, CUT, CALL)                                         \
@@ -1454,7 +1561,7 @@ int ascan_forward(const void* gates, const void* tokens, void* tokens_out, void*
   const int64_t n = num_channels * seq_total;
   if (n == 0 || num_seq == 0) return ASCAN_OK;
   Workspace w;
-  rc = carve(workspace, workspace_bytes, n, w);
+  rc = carve(workspace, workspace_bytes, num_channels, seq_total, w);
   if (rc != ASCAN_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(w.ticket, 0, w.clear_bytes, s) != cudaSuccess) return ASCAN_ECUDA;
@@ -1480,7 +1587,7 @@ int ascan_backward(const void* grad, const void* gates, const void* states, void
   const int64_t n = num_channels * seq_total;
   if (n == 0 || num_seq == 0) return ASCAN_OK;
   Workspace w;
-  rc = carve(workspace, workspace_bytes, n, w);
+  rc = carve(workspace, workspace_bytes, num_channels, seq_total, w);
   if (rc != ASCAN_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(w.ticket, 0, w.clear_bytes, s) != cudaSuccess) return ASCAN_ECUDA;
@@ -1503,7 +1610,7 @@ int ascan_forward_slab(const void* gates, const void* tokens, void* tokens_out, 
   const int64_t n = num_channels * seq_total;
   if (n == 0 || num_seq == 0) return ASCAN_OK;
   Workspace w;
-  rc = carve(workspace, workspace_bytes, n, w);
+  rc = carve(workspace, workspace_bytes, num_channels, seq_total, w);
   if (rc != ASCAN_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(w.ticket, 0, w.clear_bytes, s) != cudaSuccess) return ASCAN_ECUDA;
@@ -1531,7 +1638,7 @@ int ascan_backward_slab(const void* grad, const void* gates, const void* states,
   const int64_t n = num_channels * seq_total;
   if (n == 0 || num_seq == 0) return ASCAN_OK;
   Workspace w;
-  rc = carve(workspace, workspace_bytes, n, w);
+  rc = carve(workspace, workspace_bytes, num_channels, seq_total, w);
   if (rc != ASCAN_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(w.ticket, 0, w.clear_bytes, s) != cudaSuccess) return ASCAN_ECUDA;
@@ -1590,13 +1697,14 @@ int ascan_forward_noalloc(const void* gates, const void* tokens, void* tokens_ou
   if (!gates || !tokens || !tokens_out) return ASCAN_EINVAL;
   const int64_t n = num_channels * seq_total;
   if (n == 0 || num_seq == 0) return ASCAN_OK;
-  if (workspace_bytes_for(n) > kNoAllocScratchBytes) return ASCAN_ETOOLARGE;
+  if (workspace_bytes_for(num_channels, seq_total, false) > kNoAllocScratchBytes)
+    return ASCAN_ETOOLARGE;
   int device = -1;
   if (cudaGetDevice(&device) != cudaSuccess) return ASCAN_EDEVICE;
   void* ws = noalloc_scratch(device, &rc);
   if (ws == nullptr) return rc;
   Workspace w;
-  rc = carve(ws, kNoAllocScratchBytes, n, w);
+  rc = carve(ws, kNoAllocScratchBytes, num_channels, seq_total, w);
   if (rc != ASCAN_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the previous call's tickets and tile flags are still in the array

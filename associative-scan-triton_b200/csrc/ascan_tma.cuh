@@ -182,6 +182,8 @@ struct StageMeta {
   int64_t p0;          // flat index of the tile's first element
   float halo[2];       // bwd: [0] gate neighbour, [1] state neighbour at the tile edge
   uint32_t halo_bulk;  // bit k: halo k is in halo_raw[k] instead of halo[k]
+  uint32_t halo_idx[2];  // ragged rows: element of halo_raw[k] that is the neighbour
+  uint32_t shift;      // ragged rows: elements between the buffer start and the tile start
   // bwd: the 16-byte block holding halo k, fetched by a bulk copy with the tile
   // (the block starting at the element after the tile, or ending at the
   // element before it)
@@ -209,6 +211,7 @@ struct TileSched {
   uint32_t rows;            // row mode: C
   uint32_t tiles_per_row;   // row mode: ceil(BL / kTileElems)
   uint32_t stride;          // ticket distance to the scan predecessor
+  uint32_t ragged;          // row mode with BL not a multiple of the tile (last tile of a row partial)
 };
 
 // Hand-off slots between the consumer warps of one tile (no CTA barrier): the
@@ -223,10 +226,19 @@ struct XSlot {
   float4 te;                    // tile carry-in {a, b, flags bits, ticket bits}
 };
 
-template <int NIN, int NOUT, int NS, typename T>
+// RG (ragged rows): a tile may start anywhere inside a 128-byte TMA row, so
+// each input buffer holds one more TMA row (padded to the 1024-byte swizzle
+// atom) and the tile's elements sit `shift` elements into it.
+template <typename T, bool RG>
+constexpr int in_bytes() {
+  return Fmt<T>::kBytes + (RG ? 1024 : 0);
+}
+
+template <int NIN, int NOUT, int NS, typename T, bool RG = false>
 struct Smem {
-  alignas(1024) uint8_t in[NS][NIN][Fmt<T>::kBytes];
-  alignas(1024) uint8_t out[2][NOUT][Fmt<T>::kBytes];
+  alignas(1024) uint8_t in[NS][NIN][in_bytes<T, RG>()];
+  // output staging for the TMA stores; ragged tiles store straight from registers
+  alignas(1024) uint8_t out[2][NOUT][RG ? 16 : Fmt<T>::kBytes];
   StageMeta<NIN, T> meta[NS];
   uint64_t full[NS];
   uint64_t empty[NS];
@@ -235,9 +247,9 @@ struct Smem {
   int abort;  // a consumer warp gave up: the others stop waiting on it
 };
 
-template <int NIN, int NOUT, int NS, typename T>
+template <int NIN, int NOUT, int NS, typename T, bool RG = false>
 constexpr size_t smem_bytes() {
-  return sizeof(Smem<NIN, NOUT, NS, T>) + 1024;  // + alignment slack
+  return sizeof(Smem<NIN, NOUT, NS, T, RG>) + 1024;  // + alignment slack
 }
 
 template <typename Sm>
@@ -368,12 +380,13 @@ __device__ void build_meta(StageMeta<NIN, T>& m, const CuView<IdxT>& cu, int64_t
 // consumer helpers
 // ---------------------------------------------------------------------------
 
-// Element e of input k of the current tile, as float.
+// Element e of input k of the current tile, as float (`shift`: elements
+// between the buffer start and the tile start, ragged rows only).
 template <typename T, int NIN>
 __device__ __forceinline__ float tile_elem(const uint8_t* buf, const StageMeta<NIN, T>& m, int k,
                                            uint32_t e, uint32_t n_tma, uint32_t n_valid,
-                                           float fill) {
-  if (e < n_tma) return Cvt<T>::to(*reinterpret_cast<const T*>(buf + swz<T>(e)));
+                                           float fill, uint32_t shift = 0u) {
+  if (e < n_tma) return Cvt<T>::to(*reinterpret_cast<const T*>(buf + swz<T>(e + shift)));
   if (e < n_valid) return m.tail[k][e - n_tma];
   return fill;
 }
@@ -408,6 +421,55 @@ __device__ __forceinline__ void read_block(const uint8_t* buf, const ThreadChunk
   }
 }
 
+// This thread's 16 elements of a tile that starts `shift` elements into the
+// buffer (ragged rows): kChunks+1 aligned 16-byte chunks are read and the 16
+// elements taken from offset r = shift % kVec, which is the same for every
+// thread of the tile (a warp-uniform switch, so no register is indexed at run
+// time).
+template <typename T, int R>
+__device__ __forceinline__ void take_shifted(const float (&raw)[kPerThread + 16 / sizeof(T)],
+                                             float (&v)[kPerThread]) {
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) v[j] = raw[R + j];
+}
+
+template <typename T, int NIN>
+__device__ __forceinline__ void read_block_shifted(const uint8_t* buf, const StageMeta<NIN, T>& m,
+                                                   int k, uint32_t o, uint32_t shift,
+                                                   uint32_t n_tma, uint32_t n_valid, float fill,
+                                                   float (&v)[kPerThread]) {
+  constexpr int kVec = ThreadChunks<T>::kVec;
+  constexpr int kChunks = ThreadChunks<T>::kChunks;
+  if (o + kPerThread <= n_tma) {
+    const uint32_t r = shift % kVec;
+    const uint32_t base = o + shift - r;
+    float raw[kPerThread + kVec];
+#pragma unroll
+    for (int c = 0; c <= kChunks; ++c)
+      unpack16<T>(*reinterpret_cast<const uint4*>(buf + swz<T>(base + c * kVec)), &raw[c * kVec]);
+    switch (r) {
+      case 0: take_shifted<T, 0>(raw, v); break;
+      case 1: take_shifted<T, 1>(raw, v); break;
+      case 2: take_shifted<T, 2>(raw, v); break;
+      case 3: take_shifted<T, 3>(raw, v); break;
+      default:
+        if constexpr (kVec > 4) {
+          switch (r) {
+            case 4: take_shifted<T, (kVec > 4 ? 4 : 0)>(raw, v); break;
+            case 5: take_shifted<T, (kVec > 4 ? 5 : 0)>(raw, v); break;
+            case 6: take_shifted<T, (kVec > 4 ? 6 : 0)>(raw, v); break;
+            default: take_shifted<T, (kVec > 4 ? 7 : 0)>(raw, v); break;
+          }
+        }
+        break;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j)
+      v[j] = tile_elem<T, NIN>(buf, m, k, o + j, n_tma, n_valid, fill, shift);
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void write_block(uint8_t* buf, const ThreadChunks<T>& tc,
                                             const float (&v)[kPerThread]) {
@@ -423,6 +485,60 @@ __device__ __forceinline__ void store_direct(T* base, int64_t p, uint32_t mask,
 #pragma unroll
   for (int j = 0; j < kPerThread; ++j)
     if ((mask >> j) & 1u) base[p + j] = Cvt<T>::from(v[j]);
+}
+
+// Lane t holds the 16 elements [q + 16 t, q + 16 t + 16) of a warp-contiguous
+// run whose start q lies R elements past a 16-byte boundary.  Every lane takes
+// the last R elements of its left neighbour, so that it holds the aligned
+// window [q + 16 t - R, q + 16 t - R + 16), and writes it with 16-byte stores.
+// Lane 0 writes only its own part of its first window (the R elements before
+// q are not the warp's); lane 31's last R elements go out one by one.
+// Warp-collective.
+template <typename T, int R>
+__device__ __forceinline__ void store_window(T* base, int64_t q, const float (&v)[kPerThread],
+                                             int lane) {
+  constexpr int kVec = ThreadChunks<T>::kVec, kChunks = ThreadChunks<T>::kChunks;
+  float w[kPerThread];
+#pragma unroll
+  for (int j = 0; j < R; ++j) w[j] = __shfl_up_sync(kFull, v[kPerThread - R + j], 1);
+#pragma unroll
+  for (int j = R; j < kPerThread; ++j) w[j] = v[j - R];
+  T* p = base + (q - R);
+  if (R == 0 || lane != 0) {
+    st_v4(p, pack16<T>(&w[0]));
+  } else {
+#pragma unroll
+    for (int j = R; j < kVec; ++j) p[j] = Cvt<T>::from(w[j]);
+  }
+#pragma unroll
+  for (int c = 1; c < kChunks; ++c) st_v4(p + c * kVec, pack16<T>(&w[c * kVec]));
+  if (R != 0 && lane == 31) {
+#pragma unroll
+    for (int j = kPerThread - R; j < kPerThread; ++j) base[q + j] = Cvt<T>::from(v[j]);
+  }
+}
+
+// store_window for the run's actual misalignment r = q mod (16 bytes).
+template <typename T>
+__device__ __forceinline__ void store_realigned(T* base, int64_t q, uint32_t r,
+                                                const float (&v)[kPerThread], int lane) {
+  constexpr int kVec = ThreadChunks<T>::kVec;
+  switch (r) {
+    case 0: store_window<T, 0>(base, q, v, lane); break;
+    case 1: store_window<T, 1>(base, q, v, lane); break;
+    case 2: store_window<T, 2>(base, q, v, lane); break;
+    case 3: store_window<T, 3>(base, q, v, lane); break;
+    default:
+      if constexpr (kVec > 4) {
+        switch (r) {
+          case 4: store_window<T, (kVec > 4 ? 4 : 0)>(base, q, v, lane); break;
+          case 5: store_window<T, (kVec > 4 ? 5 : 0)>(base, q, v, lane); break;
+          case 6: store_window<T, (kVec > 4 ? 6 : 0)>(base, q, v, lane); break;
+          default: store_window<T, (kVec > 4 ? 7 : 0)>(base, q, v, lane); break;
+        }
+      }
+      break;
+  }
 }
 
 // Bits j of [0, 16) with o + j < limit.

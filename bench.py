@@ -392,6 +392,78 @@ def _small_t_graph(ast, device, reps: int = 200) -> dict:
           "graph_gbs": round(STEP_BYTES_PER_ELEM * n / (graph_ms * 1e-3) / 1e9, 1)}
 
 
+def _other_configs(ast, device, reps: int = 20) -> dict:
+  """configs[2] and configs[3] through the public autograd API (device-resident
+  inputs, fwd + backward per step, CUDA events; algorithmic bytes: 3s fwd +
+  5s bwd per element and direction, s = dtype bytes)."""
+  out = {}
+
+  def timed(step):
+    for _ in range(3):
+      step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+      step()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / reps
+
+  # configs[2]: varlen, C=2048, 32 lengths ~ U[64, 8192] (seed 0), bf16 in / fp32 accumulation,
+  # gates = sigmoid(N(2, 1)), tokens ~ N(0, 1)
+  gen = torch.Generator().manual_seed(0)
+  lens = torch.randint(64, 8193, (32,), generator=gen)
+  cu = torch.cat([torch.zeros(1, dtype=torch.int64), torch.cumsum(lens, 0)]).to(device)
+  BL, C2 = int(lens.sum()), 2048
+  g = torch.sigmoid(2.0 + torch.randn(C2, BL, generator=gen)).to(device, torch.bfloat16)
+  x = torch.randn(C2, BL, generator=gen).to(device, torch.bfloat16)
+  dy = torch.randn(C2, BL, generator=gen).to(device, torch.bfloat16)
+  args = {"cu_seqlens": cu, "chunk_size": 512,
+          "grid": ast.get_grid(len(cu), int(lens.max()), 512, C2)}
+
+  def varlen_step():
+    gl = g.detach().requires_grad_(True)
+    xl = x.detach().requires_grad_(True)
+    ast.scan_causal(gl, xl, args).backward(dy)
+
+  ms = timed(varlen_step)
+  n = C2 * BL
+  out["varlen_configs2"] = {
+    "workload": f"causal fwd+bwd, C=2048, 32 sequences of seeded lengths in [64, 8192] "
+                f"(BL={BL}), bf16, scan_causal + backward",
+    "ms_per_step": round(ms, 4), "gbs": round(16 * n / (ms * 1e-3) / 1e9, 1)}
+  del g, x, dy, cu
+
+  # configs[3]: scan_bidirectional_branched, B=8, C=1536, T=2048, fp16, independent pairs
+  Tn, C3 = 2048, 1536
+  BL = B * Tn
+  gen = torch.Generator(device=device).manual_seed(4)
+  gf = torch.rand(C3, BL, device=device, generator=gen).half()
+  xf = torch.randn(C3, BL, device=device, generator=gen).half()
+  gb = torch.rand(C3, BL, device=device, generator=gen).half()
+  xb = torch.randn(C3, BL, device=device, generator=gen).half()
+  dyf = torch.randn(C3, BL, device=device, generator=gen).half()
+  dyb = torch.randn(C3, BL, device=device, generator=gen).half()
+  cu = torch.arange(B + 1, device=device, dtype=torch.int32) * Tn
+  args = {"cu_seqlens": cu, "chunk_size": 128, "grid": ast.get_grid(len(cu), Tn, 128, C3)}
+
+  def bidi_step():
+    ins = [t.detach().requires_grad_(True) for t in (gf, xf, gb, xb)]
+    yf, yb = ast.scan_bidirectional_branched(*ins, args)
+    torch.autograd.backward([yf, yb], [dyf, dyb])
+
+  ms = timed(bidi_step)
+  n = C3 * BL
+  out["bidi_configs3"] = {
+    "workload": "scan_bidirectional_branched fwd+bwd, B=8 x T=2048, C=1536, fp16, "
+                "independent gate/token pairs per direction",
+    "ms_per_step": round(ms, 4), "gbs": round(2 * 16 * n / (ms * 1e-3) / 1e9, 1)}
+  from associative_scan_triton import _lib
+  _lib.check_device_error(device)
+  return out
+
+
 def _cpu_baseline(seconds: float = 10.0) -> dict:
   """The reference's CPU algorithm (fp64 sequential scan, oracle port) on a channel sample."""
   from oracle import oracle
@@ -540,6 +612,7 @@ def run_ours(args) -> dict | None:
   if not args.no_sweep and world == 1:
     line["sweep_B8_C1536_fp32"] = _sweep(ast, device)
     line["small_t_graph"] = _small_t_graph(ast, device)
+    line["other_configs"] = _other_configs(ast, device)
   if not args.no_cpu_baseline and world == 1:
     line["cpu_baseline"] = _cpu_baseline(args.cpu_seconds)
   return line

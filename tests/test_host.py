@@ -46,6 +46,10 @@ def test_workspace_size_grows_with_problem():
   # one 16-byte status slot per 4096 elements plus a 256-byte header
   tiles = (1536 * 8 * 65536 + 4095) // 4096
   assert big == 256 + 16 * tiles
+  # rows that are not whole tiles: one slot per tile of every row (row order
+  # cuts each row into whole tiles and a partial last one)
+  assert lib.ascan_workspace_size(7, 4097, 0) == 256 + 16 * 7 * 2
+  assert lib.ascan_workspace_size(3, 100, 0) == 256 + 16 * 1  # flat count is larger
 
 
 def test_abi_rejects_bad_arguments_without_a_gpu():

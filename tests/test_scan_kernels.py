@@ -501,3 +501,89 @@ def test_tile_orders_match_oracle(order, C, cu_list, dtype, reverse):
   assert_close_to_gold(dg, gdg, dtype, f"{order} dg", mask=mask)
   # positions outside every sequence are never written
   assert (y[:, ~mask[0]] == 7.0).all() and (dx[:, ~mask[0]] == 7.0).all()
+
+
+RAGGED_ROW_CASES = [
+  # C, cu_seqlens -- rows that are not whole tiles: the row order cuts each
+  # row into whole tiles and a partial last one, and tiles start anywhere
+  # inside a 128-byte line
+  (3, [0, 5000]),
+  (7, [0, 4097]),                     # the array ends inside a 128-byte line
+  (33, [0, 1, 5000, 9001]),
+  (2, [100, 300, 12289]),             # positions before cu[0] lie in no sequence
+  (1, [0, 70001]),                    # one long row: a chain of 18 tiles
+  (200, [0, 4100]),                   # more tiles than CTAs, tiny last tiles
+  (5, [0, 4096 * 2 + 31, 4096 * 3]),
+]
+
+
+@pytest.mark.parametrize(("C", "cu_list"), RAGGED_ROW_CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("reverse", [False, True])
+@pytest.mark.parametrize("inplace", [False, True])
+def test_ragged_row_order_matches_oracle(C, cu_list, dtype, reverse, inplace):
+  from associative_scan_triton import _lib
+  BL = cu_list[-1]
+  S = len(cu_list) - 1
+  g, x = make_inputs(C, BL, dtype=dtype, gate="long", seed=C + BL + S)
+  cu = torch.tensor(cu_list, dtype=torch.int32, device=DEV)
+  mask = in_sequence_mask(C, BL, cu)
+  dy = torch.randn(C, BL, generator=torch.Generator().manual_seed(6)).to(DEV, dtype)
+  try:
+    _lib.set_implementation("tma-row")
+    y = x.clone() if inplace else torch.full_like(x, 7.0)
+    gp = g.clone()
+    ast.forward_scan_full(gp, y if inplace else x, cu, (S, 1, C), REVERSE=reverse,
+                          CHUNK_SIZE=2, TESTING=True, tokens_out=y)
+    dx, dg = torch.full_like(x, 7.0), torch.full_like(x, 7.0)
+    ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, (S, 1, C), CHUNK_SIZE=2,
+                                 CAUSAL=not reverse)
+    torch.cuda.synchronize()
+  finally:
+    _lib.set_implementation("auto")
+  _lib.check_device_error()
+  gold_y, gold_a = oracle.scan_fwd(g, x, cu, reverse=reverse)
+  assert_close_to_gold(y, gold_y, dtype, "ragged rows y", mask=mask)
+  assert_close_to_gold(gp, gold_a, dtype, "ragged rows gate products", mask=mask)
+  gdx, gdg = oracle.scan_bwd(dy, g, y, cu, causal=not reverse)
+  assert_close_to_gold(dx, gdx, dtype, "ragged rows dx", mask=mask)
+  assert_close_to_gold(dg, gdg, dtype, "ragged rows dg", mask=mask)
+  assert (dx[:, ~mask[0]] == 7.0).all() and (dg[:, ~mask[0]] == 7.0).all()
+  if not inplace:
+    assert (y[:, ~mask[0]] == 7.0).all()
+
+
+@pytest.mark.parametrize("reverse", [False, True])
+def test_flat_sized_workspace_is_accepted(reverse):
+  """A caller that sized the workspace for the flat tile order (one status
+  slot per 4096 elements) still gets correct results: the library then keeps
+  the flat order instead of cutting ragged rows."""
+  import ctypes
+
+  from associative_scan_triton import _lib
+  C, BL = 9, 5000
+  g, x = make_inputs(C, BL, gate="long", seed=11)
+  cu = torch.tensor([0, BL], dtype=torch.int64, device=DEV)
+  f32 = _lib.DTYPE_CODES[torch.float32]
+  flat_bytes = 256 + 16 * ((C * BL + 4095) // 4096)
+  assert flat_bytes < _lib.load().ascan_workspace_size(C, BL, f32)
+  ws = torch.empty(flat_bytes, dtype=torch.uint8, device=DEV)
+  y = torch.empty_like(x)
+  stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+  def call(nbytes):
+    return _lib.load().ascan_forward(
+      g.data_ptr(), x.data_ptr(), y.data_ptr(), None, cu.data_ptr(), _lib.INDEX_CODES[cu.dtype],
+      1, C, BL, f32, int(reverse), ws.data_ptr(), nbytes, stream)
+
+  try:
+    _lib.set_implementation("tma-row")
+    rc = call(flat_bytes)
+    torch.cuda.synchronize()
+  finally:
+    _lib.set_implementation("auto")
+  assert rc == 0, _lib.strerror(rc)
+  _lib.check_device_error()
+  gold_y, _ = oracle.scan_fwd(g, x, cu, reverse=reverse)
+  assert_close_to_gold(y, gold_y, torch.float32, "flat-sized workspace")
+  assert call(flat_bytes - 1) == -2  # ASCAN_EWORKSPACE: one byte short of the flat size
