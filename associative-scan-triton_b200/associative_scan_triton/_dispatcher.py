@@ -62,3 +62,26 @@ def backward_scan_fused_full(
   num_seq, _num_chunks, no_channels = grid
   _lib.backward(grad, gates, states, d_tokens_out, d_gates_out, cu_seqlens,
                 num_seq=num_seq, num_channels=no_channels, causal=bool(CAUSAL))
+
+
+def forward_scan_full_bidi(gates_fwd, tokens_fwd, out_fwd, gates_bwd, tokens_bwd, out_bwd,
+                           cu_seqlens, grid: tuple, CHUNK_SIZE, NUM_STAGES=None) -> None:
+  """``forward_scan_full(REVERSE=False, TESTING=False)`` on the *_fwd pair and
+  ``forward_scan_full(REVERSE=True, TESTING=False)`` on the *_bwd pair, as
+  one launch (the two calls of the reference's
+  ``ScanBidirectionalBranched.forward``, scan_eager.py:122-131)."""
+  assert len(cu_seqlens) - 1 == grid[0], "cu_seqlens do not match grid configuration"
+  _lib.forward_bidi(gates_fwd, tokens_fwd, out_fwd, gates_bwd, tokens_bwd, out_bwd, cu_seqlens,
+                    num_seq=grid[0], num_channels=grid[2])
+
+
+def backward_scan_fused_full_bidi(grad_fwd, gates_fwd, states_fwd, d_tokens_fwd, d_gates_fwd,
+                                  grad_bwd, gates_bwd, states_bwd, d_tokens_bwd, d_gates_bwd,
+                                  cu_seqlens, grid: tuple, CHUNK_SIZE, NUM_STAGES=None) -> None:
+  """``backward_scan_fused_full(CAUSAL=True)`` on the *_fwd buffers and
+  ``backward_scan_fused_full(CAUSAL=False)`` on the *_bwd buffers, as one
+  launch (scan_eager.py:160-169 of the reference)."""
+  num_seq, _num_chunks, no_channels = grid
+  _lib.backward_bidi(grad_fwd, gates_fwd, states_fwd, d_tokens_fwd, d_gates_fwd, grad_bwd,
+                     gates_bwd, states_bwd, d_tokens_bwd, d_gates_bwd, cu_seqlens,
+                     num_seq=num_seq, num_channels=no_channels)

@@ -44,6 +44,9 @@ EXPORTED_SYMBOLS = (
   "ascan_backward",
   "ascan_forward_slab",
   "ascan_backward_slab",
+  "ascan_workspace_size_bidi",
+  "ascan_forward_bidi",
+  "ascan_backward_bidi",
   "ascan_shift_pad",
   "ascan_set_implementation",
   "ascan_get_implementation",
@@ -83,6 +86,13 @@ def _bind(lib) -> None:
   lib.ascan_backward_slab.restype = ci
   lib.ascan_backward_slab.argtypes = [p, p, p, p, p, p, ci, i64, i64, i64, ci, ci, p, p, p, p,
                                       sz, p]
+  lib.ascan_workspace_size_bidi.restype = sz
+  lib.ascan_workspace_size_bidi.argtypes = [i64, i64, ci]
+  lib.ascan_forward_bidi.restype = ci
+  lib.ascan_forward_bidi.argtypes = [p, p, p, p, p, p, p, ci, i64, i64, i64, ci, p, sz, p]
+  lib.ascan_backward_bidi.restype = ci
+  lib.ascan_backward_bidi.argtypes = [p, p, p, p, p, p, p, p, p, p, p, ci, i64, i64, i64, ci,
+                                      p, sz, p]
   lib.ascan_shift_pad.restype = ci
   lib.ascan_shift_pad.argtypes = [p, p, p, ci, i64, i64, i64, ci, ctypes.c_double, ci, ci, p]
   lib.ascan_set_implementation.restype = ci
@@ -320,6 +330,65 @@ def backward(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
       d_gates.data_ptr(), cu_seqlens.data_ptr(), INDEX_CODES[cu_seqlens.dtype], int(num_seq),
       C, BL, dcode, int(bool(causal)), ws.data_ptr(), ws.numel(), _stream_ptr(device))
   _finish(rc, "ascan_backward", device)
+
+
+def _check_pair(names_tensors, cu_seqlens, num_seq, num_channels):
+  device = _check_inputs(names_tensors, cu_seqlens, num_seq)
+  first_name, first = names_tensors[0]
+  C, BL = _layout(first, num_channels)
+  for name, t in names_tensors:
+    if _layout(t, num_channels) != (C, BL):
+      raise ValueError(f"{name} shape {tuple(t.shape)} does not match {first_name} "
+                       f"{tuple(first.shape)}")
+  return device, C, BL
+
+
+def _bidi_workspace(C: int, BL: int, dtype_code: int, device) -> torch.Tensor:
+  nbytes = int(load().ascan_workspace_size_bidi(C, BL, dtype_code))
+  return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def forward_bidi(gates_fwd: torch.Tensor, tokens_fwd: torch.Tensor, out_fwd: torch.Tensor,
+                 gates_bwd: torch.Tensor, tokens_bwd: torch.Tensor, out_bwd: torch.Tensor,
+                 cu_seqlens: torch.Tensor, num_seq: int, num_channels: int) -> None:
+  """ascan_forward_bidi: causal scan of the *_fwd pair and reverse scan of the
+  *_bwd pair in one launch."""
+  tensors = [("gates_fwd", gates_fwd), ("tokens_fwd", tokens_fwd), ("out_fwd", out_fwd),
+             ("gates_bwd", gates_bwd), ("tokens_bwd", tokens_bwd), ("out_bwd", out_bwd)]
+  device, C, BL = _check_pair(tensors, cu_seqlens, num_seq, num_channels)
+  lib = load()
+  dcode = DTYPE_CODES[tokens_fwd.dtype]
+  with torch.cuda.device(device):
+    ws = _bidi_workspace(C, BL, dcode, device)
+    rc = lib.ascan_forward_bidi(
+      gates_fwd.data_ptr(), tokens_fwd.data_ptr(), out_fwd.data_ptr(), gates_bwd.data_ptr(),
+      tokens_bwd.data_ptr(), out_bwd.data_ptr(), cu_seqlens.data_ptr(),
+      INDEX_CODES[cu_seqlens.dtype], int(num_seq), C, BL, dcode, ws.data_ptr(), ws.numel(),
+      _stream_ptr(device))
+  _finish(rc, "ascan_forward_bidi", device)
+
+
+def backward_bidi(grad_fwd: torch.Tensor, gates_fwd: torch.Tensor, states_fwd: torch.Tensor,
+                  d_tokens_fwd: torch.Tensor, d_gates_fwd: torch.Tensor,
+                  grad_bwd: torch.Tensor, gates_bwd: torch.Tensor, states_bwd: torch.Tensor,
+                  d_tokens_bwd: torch.Tensor, d_gates_bwd: torch.Tensor,
+                  cu_seqlens: torch.Tensor, num_seq: int, num_channels: int) -> None:
+  """ascan_backward_bidi: causal adjoint of the *_fwd buffers and reverse
+  adjoint of the *_bwd buffers in one launch."""
+  tensors = [("grad_fwd", grad_fwd), ("gates_fwd", gates_fwd), ("states_fwd", states_fwd),
+             ("d_tokens_fwd", d_tokens_fwd), ("d_gates_fwd", d_gates_fwd),
+             ("grad_bwd", grad_bwd), ("gates_bwd", gates_bwd), ("states_bwd", states_bwd),
+             ("d_tokens_bwd", d_tokens_bwd), ("d_gates_bwd", d_gates_bwd)]
+  device, C, BL = _check_pair(tensors, cu_seqlens, num_seq, num_channels)
+  lib = load()
+  dcode = DTYPE_CODES[grad_fwd.dtype]
+  with torch.cuda.device(device):
+    ws = _bidi_workspace(C, BL, dcode, device)
+    rc = lib.ascan_backward_bidi(
+      *[t.data_ptr() for _, t in tensors], cu_seqlens.data_ptr(),
+      INDEX_CODES[cu_seqlens.dtype], int(num_seq), C, BL, dcode, ws.data_ptr(), ws.numel(),
+      _stream_ptr(device))
+  _finish(rc, "ascan_backward_bidi", device)
 
 
 def _row_array(name: str, t: torch.Tensor | None, C: int, width: int, device) -> int | None:

@@ -94,8 +94,9 @@ def scan_bidi_fwd_op(gates_fwd: torch.Tensor, tokens_fwd: torch.Tensor, gates_bw
   out_fwd = torch.empty_like(tokens_fwd)
   out_bwd = torch.empty_like(tokens_bwd)
   n = _num_seq(cu_seqlens)
-  _lib.forward(gates_fwd, tokens_fwd, out_fwd, None, cu_seqlens, n, no_channels, False)
-  _lib.forward(gates_bwd, tokens_bwd, out_bwd, None, cu_seqlens, n, no_channels, True)
+  # both branches in one launch (ascan_forward_bidi)
+  _lib.forward_bidi(gates_fwd, tokens_fwd, out_fwd, gates_bwd, tokens_bwd, out_bwd, cu_seqlens, n,
+                    no_channels)
   return out_fwd, out_bwd
 
 
@@ -119,10 +120,9 @@ def scan_bidi_bwd_op(grad_fwd: torch.Tensor, grad_bwd: torch.Tensor, states_fwd:
   d_tokens_bwd = torch.empty_like(grad_bwd)
   d_gates_bwd = torch.empty_like(gates_bwd)
   n = _num_seq(cu_seqlens)
-  _lib.backward(grad_fwd, gates_fwd, states_fwd, d_tokens_fwd, d_gates_fwd, cu_seqlens, n,
-                no_channels, True)
-  _lib.backward(grad_bwd, gates_bwd, states_bwd, d_tokens_bwd, d_gates_bwd, cu_seqlens, n,
-                no_channels, False)
+  # both adjoints in one launch (ascan_backward_bidi)
+  _lib.backward_bidi(grad_fwd, gates_fwd, states_fwd, d_tokens_fwd, d_gates_fwd, grad_bwd,
+                     gates_bwd, states_bwd, d_tokens_bwd, d_gates_bwd, cu_seqlens, n, no_channels)
   return d_gates_fwd, d_tokens_fwd, d_gates_bwd, d_tokens_bwd
 
 

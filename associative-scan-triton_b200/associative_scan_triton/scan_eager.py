@@ -9,7 +9,12 @@ from __future__ import annotations
 
 import torch
 
-from ._dispatcher import backward_scan_fused_full, forward_scan_full
+from ._dispatcher import (
+  backward_scan_fused_full,
+  backward_scan_fused_full_bidi,
+  forward_scan_full,
+  forward_scan_full_bidi,
+)
 
 
 class ScanCausal(torch.autograd.Function):
@@ -77,10 +82,10 @@ class ScanBidirectionalBranched(torch.autograd.Function):
 
     out_fwd = torch.empty_like(tokens_fwd)
     out_bwd = torch.empty_like(tokens_bwd)
-    forward_scan_full(gates_fwd, tokens_fwd, cu_seqlens, grid, REVERSE=False,
-                      CHUNK_SIZE=chunk_size, TESTING=False, tokens_out=out_fwd)
-    forward_scan_full(gates_bwd, tokens_bwd, cu_seqlens, grid, REVERSE=True,
-                      CHUNK_SIZE=chunk_size, TESTING=False, tokens_out=out_bwd)
+    # the reference's two forward_scan_full calls (scan_eager.py:122-131), as
+    # one launch for both branches
+    forward_scan_full_bidi(gates_fwd, tokens_fwd, out_fwd, gates_bwd, tokens_bwd, out_bwd,
+                           cu_seqlens, grid, CHUNK_SIZE=chunk_size)
     if need_backward:
       ctx.grid = grid
       ctx.cu_seqlens = cu_seqlens
@@ -98,10 +103,12 @@ class ScanBidirectionalBranched(torch.autograd.Function):
     d_gates_fwd = torch.empty_like(gates_fwd)
     d_tokens_bwd = torch.empty_like(grad_output_bwd)
     d_gates_bwd = torch.empty_like(gates_bwd)
-    backward_scan_fused_full(grad_output_fwd, gates_fwd, states_fwd, d_tokens_fwd, d_gates_fwd,
-                             ctx.cu_seqlens, ctx.grid, CHUNK_SIZE=ctx.chunk_size, CAUSAL=True)
-    backward_scan_fused_full(grad_output_bwd, gates_bwd, states_bwd, d_tokens_bwd, d_gates_bwd,
-                             ctx.cu_seqlens, ctx.grid, CHUNK_SIZE=ctx.chunk_size, CAUSAL=False)
+    # the reference's two backward_scan_fused_full calls (scan_eager.py:160-169),
+    # as one launch for both adjoints
+    backward_scan_fused_full_bidi(grad_output_fwd, gates_fwd, states_fwd, d_tokens_fwd,
+                                  d_gates_fwd, grad_output_bwd, gates_bwd, states_bwd,
+                                  d_tokens_bwd, d_gates_bwd, ctx.cu_seqlens, ctx.grid,
+                                  CHUNK_SIZE=ctx.chunk_size)
     return d_gates_fwd, d_tokens_fwd, d_gates_bwd, d_tokens_bwd, None, None
 
 

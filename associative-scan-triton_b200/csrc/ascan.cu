@@ -428,7 +428,7 @@ constexpr int ring_depth() {
 
 // Producer warp of both kernels: TMA loads and per-tile metadata.  Tickets
 // are dealt round-robin in scan order (CTA b takes tickets b, b+G, b+2G, ...,
-// G = gridDim.x) and the launch is cooperative, so every CTA is resident and
+// G = the launch's CTAs for this scan) and the launch is cooperative, so every CTA is resident and
 // the CTAs move through the tickets in waves: a tile's predecessor is in the
 // same or an earlier wave.  In row mode the producer also copies the status
 // slot of the tile's predecessor (many waves older when rows >> CTAs) into the
@@ -456,12 +456,14 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, RG>& sm
 #pragma unroll
   for (int s = 0; s < NS; ++s) pending[s] = false, last_parity[s] = 0;
   const int64_t BL = cu.BL;
-  const uint32_t G = gridDim.x;
+  // this launch's CTAs for this scan: all of them, or one group of a
+  // bidirectional launch (CTAs [cta0, cta0 + ctas))
+  const uint32_t G = sch.ctas ? sch.ctas : gridDim.x;
   const uint32_t num_tiles = sch.num_tiles;
   // flat mode: row position of the current tile's first element, advanced by
   // the (constant) distance between this CTA's consecutive tiles
   const int64_t step = (static_cast<int64_t>(G) * kTileElems) % BL;
-  uint32_t ticket = blockIdx.x;
+  uint32_t ticket = blockIdx.x - sch.cta0;
   int64_t t_flat = 0;
   if (!sch.row_mode && ticket < num_tiles) {
     const uint32_t tile0 = REV ? num_tiles - 1u - ticket : ticket;
@@ -557,13 +559,14 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, RG>& sm
 
 // IO: the launch serves a time slab (RowIO in use or no outputs); compiled
 // separately so the ordinary kernels carry none of that code.
+// The CTA's part of one forward launch; the tensor maps are kernel
+// parameters (__grid_constant__), passed by address.
 template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO, bool RG>
-__global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
-    scan_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_g,
-                        const __grid_constant__ CUtensorMap map_x,
-                        const __grid_constant__ CUtensorMap map_y,
-                        const __grid_constant__ CUtensorMap map_gout, const FwdArgs<T, IdxT> args,
-                        int64_t n_tma_total, const tma::TileSched sch) {
+__device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUtensorMap* map_x,
+                                             const CUtensorMap* map_y,
+                                             const CUtensorMap* map_gout,
+                                             const FwdArgs<T, IdxT>& args, int64_t n_tma_total,
+                                             const tma::TileSched& sch) {
   using namespace tma;
   constexpr int NIN = 2, NOUT = GATES_OUT ? 2 : 1;
   using Sm = Smem<NIN, NOUT, NS, T, RG>;
@@ -590,7 +593,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
   const CuView<IdxT> cu{args.cu, cache_cu ? sm.cu : nullptr, S, BL};
 
   if (warp == kConsumerWarps) {
-    const CUtensorMap* maps[NIN] = {&map_g, &map_x};
+    const CUtensorMap* maps[NIN] = {map_g, map_x};
     run_producer<T, IdxT, REV, NIN, NOUT, NS, RG>(
         sm, maps, cu, N, n_tma_total, sch, args.st, lane,
         [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
@@ -603,7 +606,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     return;
   }
 
-  if (blockIdx.x == 0) validate_cu(args.cu, S, BL);
+  if (blockIdx.x == sch.cta0) validate_cu(args.cu, S, BL);
   const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
   const ThreadChunks<T> tc(o);
   const uint32_t bit_word = o >> 5, bit_shift = o & 31u;
@@ -714,8 +717,8 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     if (lane == 0) {
       if (slice_tma) {
         const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow) + warp * kPartRows;
-        tma_store_2d(&map_y, 0, row, sm.out[obuf][0] + warp * kPartBytes);
-        if constexpr (GATES_OUT) tma_store_2d(&map_gout, 0, row, sm.out[obuf][1] + warp * kPartBytes);
+        tma_store_2d(map_y, 0, row, sm.out[obuf][0] + warp * kPartBytes);
+        if constexpr (GATES_OUT) tma_store_2d(map_gout, 0, row, sm.out[obuf][1] + warp * kPartBytes);
       }
       bulk_commit();
     }
@@ -730,14 +733,14 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
   if (lane == 0) bulk_wait_all();
 }
 
+// The CTA's part of one backward launch (tensor maps passed by address, as
+// in fwd_tma_body).
 template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO, bool RG>
-__global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
-    scan_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dy,
-                        const __grid_constant__ CUtensorMap map_g,
-                        const __grid_constant__ CUtensorMap map_h,
-                        const __grid_constant__ CUtensorMap map_dx,
-                        const __grid_constant__ CUtensorMap map_dg, const BwdArgs<T, IdxT> args,
-                        int64_t n_tma_total, const tma::TileSched sch) {
+__device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CUtensorMap* map_g,
+                                             const CUtensorMap* map_h, const CUtensorMap* map_dx,
+                                             const CUtensorMap* map_dg,
+                                             const BwdArgs<T, IdxT>& args, int64_t n_tma_total,
+                                             const tma::TileSched& sch) {
   using namespace tma;
   constexpr bool REV = CAUSAL;
   constexpr int NIN = 3, NOUT = 2;
@@ -765,7 +768,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
   const CuView<IdxT> cu{args.cu, cache_cu ? sm.cu : nullptr, S, BL};
 
   if (warp == kConsumerWarps) {
-    const CUtensorMap* maps[NIN] = {&map_dy, &map_g, &map_h};
+    const CUtensorMap* maps[NIN] = {map_dy, map_g, map_h};
     run_producer<T, IdxT, REV, NIN, NOUT, NS, RG>(
         sm, maps, cu, N, n_tma_total, sch, args.st, lane,
         [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
@@ -819,7 +822,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     return;
   }
 
-  if (blockIdx.x == 0) validate_cu(args.cu, S, BL);
+  if (blockIdx.x == sch.cta0) validate_cu(args.cu, S, BL);
   const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
   const ThreadChunks<T> tc(o);
   const uint32_t bit_word = o >> 5, bit_shift = o & 31u;
@@ -970,8 +973,8 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     if (lane == 0) {
       if (slice_tma) {
         const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow) + warp * kPartRows;
-        tma_store_2d(&map_dx, 0, row, sm.out[obuf][0] + warp * kPartBytes);
-        tma_store_2d(&map_dg, 0, row, sm.out[obuf][1] + warp * kPartBytes);
+        tma_store_2d(map_dx, 0, row, sm.out[obuf][0] + warp * kPartBytes);
+        tma_store_2d(map_dg, 0, row, sm.out[obuf][1] + warp * kPartBytes);
       }
       bulk_commit();
     }
@@ -984,6 +987,74 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     set_aborted(args.st);
   }
   if (lane == 0) bulk_wait_all();
+}
+
+template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO, bool RG>
+__global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
+    scan_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_g,
+                        const __grid_constant__ CUtensorMap map_x,
+                        const __grid_constant__ CUtensorMap map_y,
+                        const __grid_constant__ CUtensorMap map_gout, const FwdArgs<T, IdxT> args,
+                        int64_t n_tma_total, const tma::TileSched sch) {
+  fwd_tma_body<T, IdxT, REV, GATES_OUT, NS, IO, RG>(&map_g, &map_x, &map_y, &map_gout, args,
+                                                    n_tma_total, sch);
+}
+
+template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO, bool RG>
+__global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
+    scan_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dy,
+                        const __grid_constant__ CUtensorMap map_g,
+                        const __grid_constant__ CUtensorMap map_h,
+                        const __grid_constant__ CUtensorMap map_dx,
+                        const __grid_constant__ CUtensorMap map_dg, const BwdArgs<T, IdxT> args,
+                        int64_t n_tma_total, const tma::TileSched sch) {
+  bwd_tma_body<T, IdxT, CAUSAL, NS, IO, RG>(&map_dy, &map_g, &map_h, &map_dx, &map_dg, args,
+                                            n_tma_total, sch);
+}
+
+// Both directions of a bidirectional scan in one launch: CTAs [0, bs.cta0)
+// run the causal branch over (gates_fwd, tokens_fwd), the others the reverse
+// branch over (gates_bwd, tokens_bwd).  The two groups share nothing (own
+// tickets, status slots and abort words); the launch is cooperative, so both
+// groups are resident and each moves through its own tickets as a separate
+// launch would.
+template <typename T, typename IdxT, int NS, bool RG>
+__global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
+    scan_fwd_bidi_tma_kernel(const __grid_constant__ CUtensorMap f_g,
+                             const __grid_constant__ CUtensorMap f_x,
+                             const __grid_constant__ CUtensorMap f_y,
+                             const __grid_constant__ CUtensorMap b_g,
+                             const __grid_constant__ CUtensorMap b_x,
+                             const __grid_constant__ CUtensorMap b_y, const FwdArgs<T, IdxT> fa,
+                             const FwdArgs<T, IdxT> ba, int64_t n_tma_total,
+                             const tma::TileSched fs, const tma::TileSched bs) {
+  if (blockIdx.x < bs.cta0)
+    fwd_tma_body<T, IdxT, false, false, NS, false, RG>(&f_g, &f_x, &f_y, &f_y, fa, n_tma_total, fs);
+  else
+    fwd_tma_body<T, IdxT, true, false, NS, false, RG>(&b_g, &b_x, &b_y, &b_y, ba, n_tma_total, bs);
+}
+
+// Adjoint of scan_fwd_bidi_tma_kernel: the causal adjoint on CTAs [0, bs.cta0),
+// the reverse adjoint on the others.
+template <typename T, typename IdxT, int NS, bool RG>
+__global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
+    scan_bwd_bidi_tma_kernel(const __grid_constant__ CUtensorMap f_dy,
+                             const __grid_constant__ CUtensorMap f_g,
+                             const __grid_constant__ CUtensorMap f_h,
+                             const __grid_constant__ CUtensorMap f_dx,
+                             const __grid_constant__ CUtensorMap f_dg,
+                             const __grid_constant__ CUtensorMap b_dy,
+                             const __grid_constant__ CUtensorMap b_g,
+                             const __grid_constant__ CUtensorMap b_h,
+                             const __grid_constant__ CUtensorMap b_dx,
+                             const __grid_constant__ CUtensorMap b_dg, const BwdArgs<T, IdxT> fa,
+                             const BwdArgs<T, IdxT> ba, int64_t n_tma_total,
+                             const tma::TileSched fs, const tma::TileSched bs) {
+  if (blockIdx.x < bs.cta0)
+    bwd_tma_body<T, IdxT, true, NS, false, RG>(&f_dy, &f_g, &f_h, &f_dx, &f_dg, fa, n_tma_total, fs);
+  else
+    bwd_tma_body<T, IdxT, false, NS, false, RG>(&b_dy, &b_g, &b_h, &b_dx, &b_dg, ba, n_tma_total,
+                                                bs);
 }
 
 // ---------------------------------------------------------------------------
@@ -1193,12 +1264,9 @@ static int sm_count() {
   return n;
 }
 
-// Cooperative launch of a persistent TMA kernel: one CTA per SM that can hold
-// it (never more CTAs than tiles).  Co-residency of every CTA is what makes the
-// round-robin tile schedule safe.  1: launched, 0: not possible here (the
-// caller falls back to the plain kernel), <0: error.
-static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles, void** params,
-                              cudaStream_t s) {
+// CTAs of `kern` that fit on the device at once (0: none, <0: error); the
+// shared-memory opt-in and the occupancy query run once per kernel and device.
+static int coop_capacity(const void* kern, size_t smem) {
   // Per kernel and device: the shared-memory opt-in and the occupancy query
   // run once (they are host-side driver calls, not free at small sizes).
   struct Entry {
@@ -1207,7 +1275,7 @@ static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles,
     int per_sm;
   };
   static std::mutex mu;
-  static Entry cache[64];
+  static Entry cache[256];
   static int n_cache = 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -1225,13 +1293,18 @@ static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles,
         cudaSuccess)
       return 0;
     std::lock_guard<std::mutex> lock(mu);
-    if (n_cache < 64) cache[n_cache++] = Entry{kern, dev, per_sm};
+    if (n_cache < 256) cache[n_cache++] = Entry{kern, dev, per_sm};
   }
   if (per_sm <= 0) return 0;
   const int sms = sm_count();
   if (sms <= 0) return 0;
-  const uint32_t resident = static_cast<uint32_t>(sms) * static_cast<uint32_t>(per_sm);
-  const uint32_t grid = num_tiles < resident ? num_tiles : resident;
+  return sms * per_sm;
+}
+
+// Cooperative launch of `grid` CTAs (at most the capacity).  1: launched,
+// <0: error.
+static int launch_coop_grid(const void* kern, size_t smem, uint32_t grid, void** params,
+                            cudaStream_t s) {
   // cooperative through the launch attribute: also valid under stream capture
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -1252,6 +1325,37 @@ static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles,
   return 1;
 }
 
+// Cooperative launch of a persistent TMA kernel: one CTA per SM that can hold
+// it (never more CTAs than tiles).  Co-residency of every CTA is what makes the
+// round-robin tile schedule safe.  1: launched, 0: not possible here (the
+// caller falls back to the plain kernel), <0: error.
+static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles, void** params,
+                              cudaStream_t s) {
+  const int cap = coop_capacity(kern, smem);
+  if (cap <= 0) return cap;
+  const uint32_t resident = static_cast<uint32_t>(cap);
+  const uint32_t grid = num_tiles < resident ? num_tiles : resident;
+  return launch_coop_grid(kern, smem, grid, params, s);
+}
+
+// Splits a cooperative grid between the two scans of a bidirectional launch
+// (each gets at most its tiles and half the resident CTAs).  false: fewer
+// than two CTAs fit, so the two scans run as separate launches.
+static bool split_bidi(int cap, tma::TileSched& fs, tma::TileSched& bs, uint32_t& grid) {
+  if (cap < 2) return false;
+  const uint32_t half = static_cast<uint32_t>(cap) / 2u;
+  const uint32_t gf = fs.num_tiles < half ? fs.num_tiles : half;
+  const uint32_t rest = static_cast<uint32_t>(cap) - gf;
+  const uint32_t gb = bs.num_tiles < rest ? bs.num_tiles : rest;
+  if (gf == 0 || gb == 0) return false;
+  fs.cta0 = 0u;
+  fs.ctas = gf;
+  bs.cta0 = gf;
+  bs.ctas = gb;
+  grid = gf + gb;
+  return true;
+}
+
 // Tile order of the TMA kernels: row mode needs row-aligned tiles (BL a
 // multiple of the tile) and pays off when sequences span several tiles: in
 // flat order their tiles are consecutive tickets of one wave, so every tile
@@ -1266,7 +1370,7 @@ static int launch_cooperative(const void* kern, size_t smem, uint32_t num_tiles,
 // has no slab I/O).
 static tma::TileSched make_sched(uint32_t num_tiles, int64_t N, int64_t BL, int64_t S,
                                  bool allow_ragged) {
-  tma::TileSched sch{num_tiles, 0u, 0u, 0u, 1u, 0u};
+  tma::TileSched sch{num_tiles, 0u, 0u, 0u, 1u, 0u, 0u, 0u};
   const int64_t C = BL > 0 ? N / BL : 0;
   const int mode = impl_mode();
   constexpr int64_t kT = tma::kTileElems;
@@ -1481,6 +1585,154 @@ static int bwd_typed(const void* dy, const void* g, const void* h, void* dx, voi
   return launch_status();
 }
 
+// ---- bidirectional pairs --------------------------------------------------
+
+// One cooperative launch for the two scans of a bidirectional pair (same
+// geometry and cu_seqlens, independent data).  1: launched, 0: not possible
+// here (the caller runs the two scans one after the other), <0: error.
+template <typename T, typename IdxT, bool RG>
+static int launch_fwd_bidi_sched(const FwdArgs<T, IdxT>& fa, const FwdArgs<T, IdxT>& ba,
+                                 tma::TileSched fs, tma::TileSched bs, cudaStream_t s) {
+  constexpr int NS = ring_depth<T, 2, 1, RG>();
+  constexpr size_t smem = tma::smem_bytes<2, 1, NS, T, RG>();
+  static_assert(smem <= kSmemBudget, "TMA forward ring does not fit in shared memory");
+  const int64_t rows = fa.N / tma::Fmt<T>::kElemsPerRow;
+  constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;
+  constexpr int kInRows = tma::Fmt<T>::kRows + (RG ? 1 : 0);
+  CUtensorMap fg, fx, fy, bg, bx, by;
+  if (!make_map<T>(&fg, fa.g, rows, kInRows) || !make_map<T>(&fx, fa.x, rows, kInRows) ||
+      !make_map<T>(&fy, fa.y, rows, kPart) || !make_map<T>(&bg, ba.g, rows, kInRows) ||
+      !make_map<T>(&bx, ba.x, rows, kInRows) || !make_map<T>(&by, ba.y, rows, kPart))
+    return 0;
+  const void* kern = reinterpret_cast<const void*>(scan_fwd_bidi_tma_kernel<T, IdxT, NS, RG>);
+  const int cap = coop_capacity(kern, smem);
+  if (cap <= 0) return cap;
+  uint32_t grid = 0;
+  if (!split_bidi(cap, fs, bs, grid)) return 0;
+  int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
+  FwdArgs<T, IdxT> f = fa, b = ba;
+  f.num_tiles = fs.num_tiles;
+  b.num_tiles = bs.num_tiles;
+  void* params[] = {&fg, &fx, &fy, &bg, &bx, &by, &f, &b, &n_tma_total, &fs, &bs};
+  return launch_coop_grid(kern, smem, grid, params, s);
+}
+
+template <typename T, typename IdxT, bool RG>
+static int launch_bwd_bidi_sched(const BwdArgs<T, IdxT>& fa, const BwdArgs<T, IdxT>& ba,
+                                 tma::TileSched fs, tma::TileSched bs, cudaStream_t s) {
+  constexpr int NS = ring_depth<T, 3, 2, RG>();
+  constexpr size_t smem = tma::smem_bytes<3, 2, NS, T, RG>();
+  static_assert(smem <= kSmemBudget, "TMA backward ring does not fit in shared memory");
+  const int64_t rows = fa.N / tma::Fmt<T>::kElemsPerRow;
+  constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;
+  constexpr int kInRows = tma::Fmt<T>::kRows + (RG ? 1 : 0);
+  CUtensorMap m[10];
+  const BwdArgs<T, IdxT>* both[2] = {&fa, &ba};
+  for (int d = 0; d < 2; ++d) {
+    const BwdArgs<T, IdxT>& a = *both[d];
+    CUtensorMap* md = m + 5 * d;
+    if (!make_map<T>(&md[0], a.dy, rows, kInRows) || !make_map<T>(&md[1], a.g, rows, kInRows) ||
+        !make_map<T>(&md[2], a.h, rows, kInRows) || !make_map<T>(&md[3], a.dx, rows, kPart) ||
+        !make_map<T>(&md[4], a.dg, rows, kPart))
+      return 0;
+  }
+  const void* kern = reinterpret_cast<const void*>(scan_bwd_bidi_tma_kernel<T, IdxT, NS, RG>);
+  const int cap = coop_capacity(kern, smem);
+  if (cap <= 0) return cap;
+  uint32_t grid = 0;
+  if (!split_bidi(cap, fs, bs, grid)) return 0;
+  int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
+  BwdArgs<T, IdxT> f = fa, b = ba;
+  f.num_tiles = fs.num_tiles;
+  b.num_tiles = bs.num_tiles;
+  void* params[] = {&m[0], &m[1], &m[2], &m[3], &m[4], &m[5], &m[6], &m[7], &m[8], &m[9],
+                    &f,    &b,    &n_tma_total, &fs, &bs};
+  return launch_coop_grid(kern, smem, grid, params, s);
+}
+
+// Causal scan of (gf, xf) and reverse scan of (gb, xb): one launch when the
+// persistent kernels apply, else the two scans one after the other.
+template <typename T, typename IdxT>
+static int fwd_bidi_typed(const void* gf, const void* xf, void* yf, const void* gb,
+                          const void* xb, void* yb, const void* cu, int64_t S, int64_t C,
+                          int64_t BL, const Workspace& wf, const Workspace& wb, cudaStream_t s) {
+  const int64_t N = C * BL;
+  const bool vec = aligned16(gf) && aligned16(xf) && aligned16(yf) && aligned16(gb) &&
+                   aligned16(xb) && aligned16(yb);
+  if (vec && use_tma() && N >= tma::Fmt<T>::kElemsPerRow) {
+    FwdArgs<T, IdxT> fa{}, ba{};
+    const void* in[2][2] = {{gf, xf}, {gb, xb}};
+    void* out[2] = {yf, yb};
+    const Workspace* ws[2] = {&wf, &wb};
+    FwdArgs<T, IdxT>* args[2] = {&fa, &ba};
+    for (int d = 0; d < 2; ++d) {
+      FwdArgs<T, IdxT>& a = *args[d];
+      a.g = static_cast<const T*>(in[d][0]);
+      a.x = static_cast<const T*>(in[d][1]);
+      a.y = static_cast<T*>(out[d]);
+      a.gout = nullptr;
+      a.cu = static_cast<const IdxT*>(cu);
+      a.S = S;
+      a.BL = BL;
+      a.N = N;
+      a.ticket = ws[d]->ticket;
+      a.st = ws[d]->st;
+      a.io = RowIO{nullptr, nullptr, nullptr};
+    }
+    const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(N)), N, BL, S,
+                                          wf.allow_ragged && wb.allow_ragged);
+    const int rc = sch.ragged ? launch_fwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s)
+                              : launch_fwd_bidi_sched<T, IdxT, false>(fa, ba, sch, sch, s);
+    if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
+  }
+  const int rc = fwd_typed<T, IdxT>(gf, xf, yf, nullptr, cu, S, C, BL, 0, wf, s);
+  if (rc != ASCAN_OK) return rc;
+  return fwd_typed<T, IdxT>(gb, xb, yb, nullptr, cu, S, C, BL, 1, wb, s);
+}
+
+// Causal adjoint of (dyf, gf, hf) and reverse adjoint of (dyb, gb, hb).
+template <typename T, typename IdxT>
+static int bwd_bidi_typed(const void* const (&in)[2][3], void* const (&out)[2][2], const void* cu,
+                          int64_t S, int64_t C, int64_t BL, const Workspace& wf,
+                          const Workspace& wb, cudaStream_t s) {
+  const int64_t N = C * BL;
+  bool vec = true;
+  for (int d = 0; d < 2; ++d) {
+    for (int k = 0; k < 3; ++k) vec = vec && aligned16(in[d][k]);
+    for (int k = 0; k < 2; ++k) vec = vec && aligned16(out[d][k]);
+  }
+  if (vec && use_tma() && N >= tma::Fmt<T>::kElemsPerRow) {
+    BwdArgs<T, IdxT> fa{}, ba{};
+    const Workspace* ws[2] = {&wf, &wb};
+    BwdArgs<T, IdxT>* args[2] = {&fa, &ba};
+    for (int d = 0; d < 2; ++d) {
+      BwdArgs<T, IdxT>& a = *args[d];
+      a.dy = static_cast<const T*>(in[d][0]);
+      a.g = static_cast<const T*>(in[d][1]);
+      a.h = static_cast<const T*>(in[d][2]);
+      a.dx = static_cast<T*>(out[d][0]);
+      a.dg = static_cast<T*>(out[d][1]);
+      a.cu = static_cast<const IdxT*>(cu);
+      a.S = S;
+      a.BL = BL;
+      a.N = N;
+      a.ticket = ws[d]->ticket;
+      a.st = ws[d]->st;
+      a.io = RowIO{nullptr, nullptr, nullptr};
+    }
+    const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(N)), N, BL, S,
+                                          wf.allow_ragged && wb.allow_ragged);
+    const int rc = sch.ragged ? launch_bwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s)
+                              : launch_bwd_bidi_sched<T, IdxT, false>(fa, ba, sch, sch, s);
+    if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
+  }
+  const int rc = bwd_typed<T, IdxT>(in[0][0], in[0][1], in[0][2], out[0][0], out[0][1], cu, S, C,
+                                    BL, 1, wf, s);
+  if (rc != ASCAN_OK) return rc;
+  return bwd_typed<T, IdxT>(in[1][0], in[1][1], in[1][2], out[1][0], out[1][1], cu, S, C, BL, 0,
+                            wb, s);
+}
+
 template <typename T, typename IdxT>
 static int shift_pad_typed(const void* data, void* out, const void* cu, int64_t S, int64_t C,
                            int64_t BL, double pad, int backward, int wrap, cudaStream_t s) {
@@ -1648,6 +1900,100 @@ int ascan_backward_slab(const void* grad, const void* gates, const void* states,
                   seq_total, causal, w, s, io)
   ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_BWD_CALL);
 #undef ASCAN_BWD_CALL
+}
+
+// Workspace of a bidirectional pair: two halves, one per scan, each a
+// multiple of 256 bytes.
+static size_t bidi_half_bytes(int64_t C, int64_t BL) {
+  const size_t b = (C <= 0 || BL <= 0) ? 256 : workspace_bytes_for(C, BL, true);
+  return (b + 255) & ~static_cast<size_t>(255);
+}
+
+size_t ascan_workspace_size_bidi(int64_t num_channels, int64_t seq_total, int dtype) {
+  (void)dtype;
+  return 2 * bidi_half_bytes(num_channels, seq_total);
+}
+
+// Splits and clears the workspace of a bidirectional pair.
+static int carve_bidi(void* ws, size_t ws_bytes, int64_t C, int64_t BL, Workspace& wf,
+                      Workspace& wb, cudaStream_t s) {
+  if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return ASCAN_EWORKSPACE;
+  const size_t half = (ws_bytes / 2) & ~static_cast<size_t>(255);
+  int rc = carve(ws, half, C, BL, wf);
+  if (rc != ASCAN_OK) return rc;
+  rc = carve(static_cast<char*>(ws) + half, half, C, BL, wb);
+  if (rc != ASCAN_OK) return rc;
+  if (cudaMemsetAsync(ws, 0, half + wb.clear_bytes, s) != cudaSuccess) return ASCAN_ECUDA;
+  return ASCAN_OK;
+}
+
+int ascan_forward_bidi(const void* gates_fwd, const void* tokens_fwd, void* tokens_out_fwd,
+                       const void* gates_bwd, const void* tokens_bwd, void* tokens_out_bwd,
+                       const void* cu_seqlens, int cu_index_type, int64_t num_seq,
+                       int64_t num_channels, int64_t seq_total, int dtype, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  int rc = check_common(cu_seqlens, cu_index_type, num_seq, num_channels, seq_total, dtype);
+  if (rc != ASCAN_OK) return rc;
+  if (!gates_fwd || !tokens_fwd || !tokens_out_fwd || !gates_bwd || !tokens_bwd ||
+      !tokens_out_bwd)
+    return ASCAN_EINVAL;
+  // the two scans run at the same time: neither output may be the other's input
+  if (tokens_out_fwd == tokens_out_bwd || tokens_out_fwd == gates_bwd ||
+      tokens_out_fwd == tokens_bwd || tokens_out_bwd == gates_fwd || tokens_out_bwd == tokens_fwd)
+    return ASCAN_EINVAL;
+  const int64_t n = num_channels * seq_total;
+  if (n == 0 || num_seq == 0) return ASCAN_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Workspace wf, wb;
+  rc = carve_bidi(workspace, workspace_bytes, num_channels, seq_total, wf, wb, s);
+  if (rc != ASCAN_OK) return rc;
+#define ASCAN_FWD_BIDI_CALL(T, I)                                                               \
+  fwd_bidi_typed<T, I>(gates_fwd, tokens_fwd, tokens_out_fwd, gates_bwd, tokens_bwd,            \
+                       tokens_out_bwd, cu_seqlens, num_seq, num_channels, seq_total, wf, wb, s)
+  ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_FWD_BIDI_CALL);
+#undef ASCAN_FWD_BIDI_CALL
+}
+
+int ascan_backward_bidi(const void* grad_fwd, const void* gates_fwd, const void* states_fwd,
+                        void* d_tokens_fwd, void* d_gates_fwd, const void* grad_bwd,
+                        const void* gates_bwd, const void* states_bwd, void* d_tokens_bwd,
+                        void* d_gates_bwd, const void* cu_seqlens, int cu_index_type,
+                        int64_t num_seq, int64_t num_channels, int64_t seq_total, int dtype,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_common(cu_seqlens, cu_index_type, num_seq, num_channels, seq_total, dtype);
+  if (rc != ASCAN_OK) return rc;
+  const void* const in[2][3] = {{grad_fwd, gates_fwd, states_fwd},
+                                {grad_bwd, gates_bwd, states_bwd}};
+  void* const out[2][2] = {{d_tokens_fwd, d_gates_fwd}, {d_tokens_bwd, d_gates_bwd}};
+  for (int d = 0; d < 2; ++d) {
+    for (int k = 0; k < 3; ++k)
+      if (!in[d][k]) return ASCAN_EINVAL;
+    for (int k = 0; k < 2; ++k)
+      if (!out[d][k]) return ASCAN_EINVAL;
+  }
+  // every output distinct from the other outputs and from the gates and states
+  // of both directions (the shifted reads cross thread boundaries, and the two
+  // adjoints run at the same time)
+  for (int d = 0; d < 2; ++d)
+    for (int k = 0; k < 2; ++k) {
+      const void* o = out[d][k];
+      for (int e = 0; e < 2; ++e) {
+        if (o == in[e][1] || o == in[e][2]) return ASCAN_EINVAL;
+        if (e != d && o == in[e][0]) return ASCAN_EINVAL;
+        for (int j = 0; j < 2; ++j)
+          if ((e != d || j != k) && o == out[e][j]) return ASCAN_EINVAL;
+      }
+    }
+  const int64_t n = num_channels * seq_total;
+  if (n == 0 || num_seq == 0) return ASCAN_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Workspace wf, wb;
+  rc = carve_bidi(workspace, workspace_bytes, num_channels, seq_total, wf, wb, s);
+  if (rc != ASCAN_OK) return rc;
+#define ASCAN_BWD_BIDI_CALL(T, I)                                                               \
+  bwd_bidi_typed<T, I>(in, out, cu_seqlens, num_seq, num_channels, seq_total, wf, wb, s)
+  ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_BWD_BIDI_CALL);
+#undef ASCAN_BWD_BIDI_CALL
 }
 
 int ascan_shift_pad(const void* data, void* out, const void* cu_seqlens, int cu_index_type,

@@ -212,6 +212,8 @@ struct TileSched {
   uint32_t tiles_per_row;   // row mode: ceil(BL / kTileElems)
   uint32_t stride;          // ticket distance to the scan predecessor
   uint32_t ragged;          // row mode with BL not a multiple of the tile (last tile of a row partial)
+  uint32_t cta0;            // first CTA of this scan's group (0 unless bidirectional)
+  uint32_t ctas;            // CTAs of the group (0: the whole grid)
 };
 
 // Hand-off slots between the consumer warps of one tile (no CTA barrier): the

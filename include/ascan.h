@@ -202,6 +202,44 @@ ASCAN_API int ascan_backward_slab(const void* grad, const void* gates, const voi
                                   void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Bidirectional pair in one launch: the causal scan of (gates_fwd,
+ * tokens_fwd) and the reverse scan of (gates_bwd, tokens_bwd), same
+ * cu_seqlens and shape.  Replaces the two forward_scan_full calls of
+ * ScanBidirectionalBranched.forward
+ * (src/associative_scan_triton/scan_eager.py:122-131) and of the
+ * scan_bidi_fwd triton_op (src/associative_scan_triton/scan_compiled.py:208-240).
+ * When the persistent kernels apply, the launch's CTAs are split in two
+ * groups, one per scan; otherwise the two scans run one after the other.
+ * The outputs may equal their own direction's tokens (in place) but no
+ * buffer of the other direction.  workspace: ascan_workspace_size_bidi bytes.
+ */
+ASCAN_API size_t ascan_workspace_size_bidi(int64_t num_channels, int64_t seq_total, int dtype);
+ASCAN_API int ascan_forward_bidi(const void* gates_fwd, const void* tokens_fwd,
+                                 void* tokens_out_fwd, const void* gates_bwd,
+                                 const void* tokens_bwd, void* tokens_out_bwd,
+                                 const void* cu_seqlens, int cu_index_type, int64_t num_seq,
+                                 int64_t num_channels, int64_t seq_total, int dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Adjoint of ascan_forward_bidi in one launch: ascan_backward with causal = 1
+ * on the *_fwd buffers and with causal = 0 on the *_bwd buffers.  Replaces
+ * the two backward_scan_fused_full calls of
+ * ScanBidirectionalBranched.backward
+ * (src/associative_scan_triton/scan_eager.py:160-169) and the scan_bidi_bwd
+ * triton_op (src/associative_scan_triton/scan_compiled.py:243-279).  Every output must
+ * differ from every other output and from the gates and states of both
+ * directions; d_tokens may equal its own direction's grad.
+ */
+ASCAN_API int ascan_backward_bidi(const void* grad_fwd, const void* gates_fwd,
+                                  const void* states_fwd, void* d_tokens_fwd, void* d_gates_fwd,
+                                  const void* grad_bwd, const void* gates_bwd,
+                                  const void* states_bwd, void* d_tokens_bwd, void* d_gates_bwd,
+                                  const void* cu_seqlens, int cu_index_type, int64_t num_seq,
+                                  int64_t num_channels, int64_t seq_total, int dtype,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Shift by one position inside every sequence and pad the vacated slot.
  * Replaces _shift_pad_kernel / shift_pad_compiled
  * (src/associative_scan_triton/_shift_pad.py:63-165) and the torch.roll

@@ -70,6 +70,28 @@ def test_abi_rejects_bad_arguments_without_a_gpu():
   assert rc == -2
 
 
+def test_bidi_abi_refuses_crossed_buffers_without_a_gpu():
+  """The two directions of ascan_*_bidi run at the same time, so an output of
+  one may not be a buffer the other reads or writes; all checks come before
+  any CUDA call."""
+  lib = _lib.load()
+  gf, xf, yf, gb, xb, yb, cu = 16, 32, 48, 64, 80, 96, 112
+  fwd = lambda *p, ws=None: lib.ascan_forward_bidi(*p, cu, 0, 1, 1, 4, 0, ws, 0, None)
+  assert fwd(gf, xf, yf, gb, xb, xf) == -1          # reverse output over the causal tokens
+  assert fwd(gf, xf, xb, gb, xb, yb) == -1          # causal output over the reverse tokens
+  assert fwd(gf, xf, yf, gb, xb, yf) == -1          # one output for both
+  assert fwd(gf, xf, yf, gb, xb, yb) == -2          # valid shape, no workspace
+  assert fwd(gf, xf, xf, gb, xb, xb) == -2          # in place in each direction is allowed
+  dyf, hf, dxf, dgf, dyb, hb, dxb, dgb = 128, 144, 160, 176, 192, 208, 224, 240
+  bwd = lambda *p: lib.ascan_backward_bidi(*p, cu, 0, 1, 1, 4, 0, None, 0, None)
+  assert bwd(dyf, gf, hf, dxf, dgf, dyb, gb, hb, dxb, dgb) == -2
+  assert bwd(dyf, gf, hf, dxf, dgf, dyb, gb, hb, dxb, hf) == -1   # over the causal states
+  assert bwd(dyf, gf, hf, dxf, dgf, dyb, gb, hb, dyf, dgb) == -1  # over the causal grad
+  assert bwd(dyf, gf, hf, dxf, dgf, dyb, gb, hb, dxf, dgb) == -1  # two outputs in one buffer
+  assert bwd(dyf, gf, hf, dyf, dgf, dyb, gb, hb, dyb, dgb) == -2  # d_tokens over own grad: ok
+  assert lib.ascan_workspace_size_bidi(7, 4097, 0) == 2 * 512  # two 256-aligned halves
+
+
 def test_ops_refuse_cpu_tensors():
   g = torch.rand(2, 8)
   x = torch.rand(2, 8)

@@ -73,3 +73,108 @@ def test_bidi_matches_reference_golden():
          "d_gates_bwd": leaves[2].grad, "d_tokens_bwd": leaves[3].grad}
   for name, t in got.items():
     assert_close_to_gold(t, z[f"{c}/{name}"].astype(np.float64), torch.float32, name, rtol=2e-5)
+
+
+BIDI_FUSED_CASES = [
+  # C, seqlens
+  (64, [2048] * 8),          # configs[3] geometry, fewer channels
+  (33, [5000, 20000, 77]),   # look-back across tiles
+  (7, [4097]),               # ragged rows (row order, partial last tiles)
+  (300, [4096 * 3]),         # aligned row order
+  (3, [100]),                # one tile
+]
+
+
+def _bidi_inputs(C, BL, dtype, seed):
+  gen = torch.Generator().manual_seed(seed)
+  ts = [torch.rand(C, BL, generator=gen) * 0.5 + 0.5 if k % 2 == 0 else torch.randn(C, BL, generator=gen)
+        for k in range(6)]
+  return [t.to(DEV, dtype) for t in ts]  # gf, xf, gb, xb, dyf, dyb
+
+
+@pytest.mark.parametrize("impl", ["auto", "tma-flat", "simple"])
+@pytest.mark.parametrize(("C", "seqlens"), BIDI_FUSED_CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_fused_bidi_launch_matches_two_launches(impl, C, seqlens, dtype):
+  """One launch for both directions (ascan_forward_bidi / ascan_backward_bidi)
+  against the two single-direction launches it replaces; bit for bit where no
+  tile needs a look-back (the same arithmetic), else to float rounding."""
+  from associative_scan_triton import _lib
+  cu = torch.tensor([0, *np.cumsum(seqlens)], device=DEV, dtype=torch.int32)
+  S, BL = len(seqlens), int(sum(seqlens))
+  gf, xf, gb, xb, dyf, dyb = _bidi_inputs(C, BL, dtype, seed=C + BL)
+  e = torch.empty_like
+  try:
+    _lib.set_implementation(impl)
+    yf, yb = e(xf), e(xb)
+    _lib.forward_bidi(gf, xf, yf, gb, xb, yb, cu, S, C)
+    d = [e(xf) for _ in range(4)]
+    _lib.backward_bidi(dyf, gf, yf, d[0], d[1], dyb, gb, yb, d[2], d[3], cu, S, C)
+    yf2, yb2 = e(xf), e(xb)
+    _lib.forward(gf, xf, yf2, None, cu, S, C, False)
+    _lib.forward(gb, xb, yb2, None, cu, S, C, True)
+    d2 = [e(xf) for _ in range(4)]
+    _lib.backward(dyf, gf, yf2, d2[0], d2[1], cu, S, C, True)
+    _lib.backward(dyb, gb, yb2, d2[2], d2[3], cu, S, C, False)
+    torch.cuda.synchronize()
+  finally:
+    _lib.set_implementation("auto")
+  _lib.check_device_error()
+  got, want = [yf, yb, *d], [yf2, yb2, *d2]
+  if all(L <= 4096 and 4096 % L == 0 for L in seqlens):
+    for k, (a, b) in enumerate(zip(got, want)):
+      assert torch.equal(a, b), k
+  else:
+    tol = 1e-6 if dtype == torch.float32 else 1e-2
+    for a, b in zip(got, want):
+      torch.testing.assert_close(a.float(), b.float(), rtol=tol, atol=tol)
+  # and against the oracle, through the reference-facing API
+  oy_f, odx_f, odg_f = oracle.scan_fwd_bwd(gf, xf, dyf, cu, causal=True)
+  oy_b, odx_b, odg_b = oracle.scan_fwd_bwd(gb, xb, dyb, cu, causal=False)
+  for t, gold, name in ((yf, oy_f, "y fwd"), (yb, oy_b, "y bwd"), (d[0], odx_f, "dx fwd"),
+                        (d[1], odg_f, "dg fwd"), (d[2], odx_b, "dx bwd"), (d[3], odg_b, "dg bwd")):
+    assert_close_to_gold(t, gold, dtype, name)
+
+
+def test_fused_bidi_graph_replay():
+  """The fused launches are stream operations like the single ones: a CUDA
+  graph of one bidirectional fwd+bwd step replays to the eager result."""
+  from associative_scan_triton import _lib
+  C, seqlens = 96, [2048] * 4
+  cu = torch.tensor([0, *np.cumsum(seqlens)], device=DEV, dtype=torch.int32)
+  S, BL = len(seqlens), int(sum(seqlens))
+  ins = _bidi_inputs(C, BL, torch.float32, seed=3)
+  gf, xf, gb, xb, dyf, dyb = ins
+  outs = [torch.empty_like(xf) for _ in range(6)]
+
+  def step():
+    _lib.forward_bidi(gf, xf, outs[0], gb, xb, outs[1], cu, S, C)
+    _lib.backward_bidi(dyf, gf, outs[0], outs[2], outs[3], dyb, gb, outs[1], outs[4], outs[5],
+                       cu, S, C)
+
+  was = _lib.sync_check_enabled()
+  _lib.set_sync_check(False)
+  try:
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+      for _ in range(2):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+      step()
+    fresh = _bidi_inputs(C, BL, torch.float32, seed=4)
+    for t, f in zip(ins, fresh):
+      t.copy_(f)
+    graph.replay()
+    torch.cuda.synchronize()
+    replayed = [o.clone() for o in outs]
+    step()
+    torch.cuda.synchronize()
+    for a, b in zip(replayed, outs):
+      assert torch.equal(a, b)
+    del graph
+  finally:
+    _lib.set_sync_check(was)
+  _lib.check_device_error()
