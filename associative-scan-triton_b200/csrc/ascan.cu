@@ -426,6 +426,14 @@ constexpr int ring_depth() {
     return ring_depth<T, NIN, NOUT, RG, NS - 1>();
 }
 
+// Whether the kernels that stage their outputs for TMA stores fit with a
+// two-stage ring; when they do not (large tiles), the register-store (RG)
+// kernels serve every schedule.
+template <typename T, int NIN, int NOUT>
+constexpr bool staged_fits() {
+  return tma::smem_bytes<NIN, NOUT, 2, T, false>() <= kSmemBudget;
+}
+
 // Producer warp of both kernels: TMA loads and per-tile metadata.  Tickets
 // are dealt round-robin in scan order (CTA b takes tickets b, b+G, b+2G, ...,
 // G = the launch's CTAs for this scan) and the launch is cooperative, so every CTA is resident and
@@ -639,8 +647,8 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
       read_block<T, NIN>(sm.in[stage][1], tc, m, 1, o, n_tma, n_valid, 0.f, b);
     }
     const uint32_t head =
-        ((REV ? m.ebits[bit_word] : m.sbits[bit_word]) >> bit_shift) & 0xffffu;
-    const uint32_t omask = has_outside ? (m.obits[bit_word] >> bit_shift) & 0xffffu : 0u;
+        ((REV ? m.ebits[bit_word] : m.sbits[bit_word]) >> bit_shift) & kThreadMask;
+    const uint32_t omask = has_outside ? (m.obits[bit_word] >> bit_shift) & kThreadMask : 0u;
     const bool first_is_head =
         REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
     bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
@@ -652,7 +660,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     if (early && lane == 0) early_raw = load_status_raw(args.st, ticket - sch.stride);
     // time slabs: row ends in scan order, where the row aggregate is taken
     const uint32_t lastmask =
-        IO && args.io.agg ? ((REV ? m.sbits[bit_word] : m.ebits[bit_word]) >> bit_shift) & 0xffffu
+        IO && args.io.agg ? ((REV ? m.sbits[bit_word] : m.ebits[bit_word]) >> bit_shift) & kThreadMask
                           : 0u;
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[stage]);
@@ -671,7 +679,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     // a, b hold the local prefixes: h = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV>(head);
     if (IO && lastmask != 0u) record_row_agg<REV>(a, b, lastmask, cm, P, p0 + o, BL, args.io.agg);
-    if (__all_sync(kFull, cm == 0xffffu)) {  // warp-uniform: no lane holds a head
+    if (__all_sync(kFull, cm == kThreadMask)) {  // warp-uniform: no lane holds a head
 #pragma unroll
       for (int j = 0; j < kPerThread; ++j) {
         b[j] = fmaf(a[j], P.b, b[j]);
@@ -695,7 +703,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     const bool slice_tma =
         !RG && store && !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
     if constexpr (RG) {
-      if (__all_sync(kFull, direct == 0xffffu)) {
+      if (__all_sync(kFull, direct == kThreadMask)) {
         // ragged rows: a wholly valid warp slice leaves by realigned 16-byte stores
         const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T>::kVec);
         store_realigned<T>(args.y, p0 + o, r, b, lane);
@@ -883,9 +891,9 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
                                      shift)
                  : halo_h;
     }
-    const uint32_t smask = (m.sbits[bit_word] >> bit_shift) & 0xffffu;
-    const uint32_t emask = (m.ebits[bit_word] >> bit_shift) & 0xffffu;
-    const uint32_t omask = has_outside ? (m.obits[bit_word] >> bit_shift) & 0xffffu : 0u;
+    const uint32_t smask = (m.sbits[bit_word] >> bit_shift) & kThreadMask;
+    const uint32_t emask = (m.ebits[bit_word] >> bit_shift) & kThreadMask;
+    const uint32_t omask = has_outside ? (m.obits[bit_word] >> bit_shift) & kThreadMask : 0u;
     const bool first_is_head =
         REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
     bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
@@ -951,7 +959,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     const bool slice_tma =
         !RG && store && !has_outside && (warp + 1) * (kTileElems / kConsumerWarps) <= n_tma;
     if constexpr (RG) {
-      if (__all_sync(kFull, direct == 0xffffu)) {
+      if (__all_sync(kFull, direct == kThreadMask)) {
         // ragged rows: a wholly valid warp slice leaves by realigned 16-byte stores
         const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T>::kVec);
         store_realigned<T>(args.dx, p0 + o, r, dyv, lane);
@@ -1149,8 +1157,8 @@ struct Workspace {
 };
 
 // Tiles of the plain kernels (kTile elements) and of the persistent TMA
-// kernels (tma::kTileElems, a divisor of kTile); status slots are counted in
-// the smaller tiles so that either family fits the same workspace.
+// kernels (tma::kTileElems; one divides the other); status slots are counted
+// in the smaller tiles so that either family fits the same workspace.
 static size_t tiles_of(int64_t n) { return static_cast<size_t>((n + kTile - 1) / kTile); }
 static size_t tma_tiles_of(int64_t n) {
   return static_cast<size_t>((n + tma::kTileElems - 1) / tma::kTileElems);
@@ -1158,7 +1166,8 @@ static size_t tma_tiles_of(int64_t n) {
 // Row order with ragged rows (BL not a multiple of the tile) cuts every row
 // into ceil(BL / tile) tiles, a few more than the flat count.
 static size_t status_slots(int64_t C, int64_t BL, bool ragged) {
-  const size_t flat = tma_tiles_of(C * BL);
+  const size_t plain = tiles_of(C * BL), tma_flat = tma_tiles_of(C * BL);
+  const size_t flat = plain > tma_flat ? plain : tma_flat;  // either kernel family
   if (!ragged || BL < tma::kTileElems) return flat;  // ragged rows are at least a tile
   const size_t rows = static_cast<size_t>(C) *
                       static_cast<size_t>((BL + tma::kTileElems - 1) / tma::kTileElems);
@@ -1434,8 +1443,13 @@ static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, bool allow_ragged, cudaStre
   // ragged rows need the shifted-tile kernels, which exist without slab I/O only
   const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(a.N)), a.N, a.BL,
                                         a.S, allow_ragged && !io);
-  if (sch.ragged) return launch_fwd_tma_sched<T, IdxT, REV, GOUT, true>(a, sch, io, s);
-  return launch_fwd_tma_sched<T, IdxT, REV, GOUT, false>(a, sch, io, s);
+  constexpr bool kStaged = staged_fits<T, 2, GOUT ? 2 : 1>();
+  if (sch.ragged || !kStaged) {
+    if (io) return 0;  // slab I/O exists in the staged kernels only
+    return launch_fwd_tma_sched<T, IdxT, REV, GOUT, true>(a, sch, io, s);
+  }
+  if constexpr (kStaged) return launch_fwd_tma_sched<T, IdxT, REV, GOUT, false>(a, sch, io, s);
+  return 0;
 }
 
 template <typename T, typename IdxT, bool CAUSAL, bool RG>
@@ -1472,8 +1486,13 @@ static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, bool allow_ragged, cudaStre
   const bool io = a.io.carry || a.io.halo || a.io.agg || !a.dx;
   const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(a.N)), a.N, a.BL,
                                         a.S, allow_ragged && !io);
-  if (sch.ragged) return launch_bwd_tma_sched<T, IdxT, CAUSAL, true>(a, sch, io, s);
-  return launch_bwd_tma_sched<T, IdxT, CAUSAL, false>(a, sch, io, s);
+  constexpr bool kStaged = staged_fits<T, 3, 2>();
+  if (sch.ragged || !kStaged) {
+    if (io) return 0;  // slab I/O exists in the staged kernels only
+    return launch_bwd_tma_sched<T, IdxT, CAUSAL, true>(a, sch, io, s);
+  }
+  if constexpr (kStaged) return launch_bwd_tma_sched<T, IdxT, CAUSAL, false>(a, sch, io, s);
+  return 0;
 }
 
 template <typename T, typename IdxT, int VEC>
@@ -1681,8 +1700,12 @@ static int fwd_bidi_typed(const void* gf, const void* xf, void* yf, const void* 
     }
     const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(N)), N, BL, S,
                                           wf.allow_ragged && wb.allow_ragged);
-    const int rc = sch.ragged ? launch_fwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s)
-                              : launch_fwd_bidi_sched<T, IdxT, false>(fa, ba, sch, sch, s);
+    int rc = 0;
+    if constexpr (staged_fits<T, 2, 1>())
+      rc = sch.ragged ? launch_fwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s)
+                      : launch_fwd_bidi_sched<T, IdxT, false>(fa, ba, sch, sch, s);
+    else
+      rc = launch_fwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
   }
   const int rc = fwd_typed<T, IdxT>(gf, xf, yf, nullptr, cu, S, C, BL, 0, wf, s);
@@ -1722,8 +1745,12 @@ static int bwd_bidi_typed(const void* const (&in)[2][3], void* const (&out)[2][2
     }
     const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(N)), N, BL, S,
                                           wf.allow_ragged && wb.allow_ragged);
-    const int rc = sch.ragged ? launch_bwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s)
-                              : launch_bwd_bidi_sched<T, IdxT, false>(fa, ba, sch, sch, s);
+    int rc = 0;
+    if constexpr (staged_fits<T, 3, 2>())
+      rc = sch.ragged ? launch_bwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s)
+                      : launch_bwd_bidi_sched<T, IdxT, false>(fa, ba, sch, sch, s);
+    else
+      rc = launch_bwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
   }
   const int rc = bwd_typed<T, IdxT>(in[0][0], in[0][1], in[0][2], out[0][0], out[0][1], cu, S, C,

@@ -43,10 +43,20 @@ constexpr int kCtasPerSm = 32 / kConsumerWarps / 4;       // 2 for 4 warps, 1 fo
 static_assert(kCtasPerSm >= 1, "4 or 8 consumer warps");
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;        // + producer warp
-constexpr int kPerThread = 16;                   // elements per consumer thread
-constexpr int kTileElems = kConsumers * kPerThread;  // 4096 (8 warps) or 2048 (4 warps)
-static_assert(kTileElems <= kTile && kTile % kTileElems == 0,
-              "TMA tiles divide the plain kernels' tiles (status slots are sized for them)");
+// Elements per consumer thread (compile-time): 16 by default; 32 doubles the
+// tile (8192 elements with 8 warps), halving the per-tile fixed costs per
+// byte at the price of shared memory (two stages, and kernels whose staged
+// outputs no longer fit store them from registers).
+#ifndef ASCAN_PER_THREAD
+#define ASCAN_PER_THREAD 16
+#endif
+constexpr int kPerThread = ASCAN_PER_THREAD;
+static_assert(kPerThread == 16 || kPerThread == 32, "16 or 32 elements per thread");
+// bits of one thread's elements in a 32-bit mask
+constexpr uint32_t kThreadMask = kPerThread == 32 ? 0xffffffffu : (1u << kPerThread) - 1u;
+constexpr int kTileElems = kConsumers * kPerThread;  // 4096 (8 warps x 16)
+static_assert(kTile % kTileElems == 0 || kTileElems % kTile == 0,
+              "TMA tiles and the plain kernels' tiles nest (status slots count the smaller)");
 constexpr int kBitWords = kTileElems / 32;
 constexpr int kCuCache = 1024;                   // cu_seqlens entries cached in smem
 constexpr uint32_t kDone = 0xffffffffu;
@@ -543,9 +553,9 @@ __device__ __forceinline__ void store_realigned(T* base, int64_t q, uint32_t r,
   }
 }
 
-// Bits j of [0, 16) with o + j < limit.
+// Bits j of [0, kPerThread) with o + j < limit.
 __device__ __forceinline__ uint32_t below_mask(uint32_t o, uint32_t limit) {
-  if (limit >= o + kPerThread) return 0xffffu;
+  if (limit >= o + kPerThread) return kThreadMask;
   return limit > o ? (1u << (limit - o)) - 1u : 0u;
 }
 
@@ -590,9 +600,9 @@ __device__ __forceinline__ Pfx fold16_inplace(float (&a)[kPerThread], float (&b)
 // take the carry-in.
 template <bool REV>
 __device__ __forceinline__ uint32_t carry_mask(uint32_t head) {
-  if (head == 0u) return 0xffffu;
+  if (head == 0u) return kThreadMask;
   if (!REV) return (1u << (__ffs(head) - 1)) - 1u;
-  return 0xffffu & ~((2u << (31 - __clz(head))) - 1u);
+  return kThreadMask & ~((2u << (31 - __clz(head))) - 1u);
 }
 
 // ---- time slabs: per-row carry-in, halo and aggregate --------------------
