@@ -50,6 +50,8 @@ EXPORTED_SYMBOLS = (
   "ascan_shift_pad",
   "ascan_set_implementation",
   "ascan_get_implementation",
+  "ascan_set_tile_width",
+  "ascan_get_tile_width",
   "ascan_get_device_error",
   "ascan_clear_device_error",
   "ascan_selftest_waits",
@@ -99,6 +101,10 @@ def _bind(lib) -> None:
   lib.ascan_set_implementation.argtypes = [ci]
   lib.ascan_get_implementation.restype = ci
   lib.ascan_get_implementation.argtypes = []
+  lib.ascan_set_tile_width.restype = ci
+  lib.ascan_set_tile_width.argtypes = [ci]
+  lib.ascan_get_tile_width.restype = ci
+  lib.ascan_get_tile_width.argtypes = []
   lib.ascan_get_device_error.restype = ci
   lib.ascan_get_device_error.argtypes = [ci, ctypes.POINTER(ctypes.c_uint),
                                          ctypes.POINTER(ctypes.c_longlong)]
@@ -162,6 +168,18 @@ def set_implementation(name: str) -> None:
   rc = load().ascan_set_implementation(IMPLEMENTATIONS[name])
   if rc != ASCAN_OK:
     raise ScanError(f"ascan_set_implementation: {strerror(rc)}")
+
+
+def set_tile_width(elems_per_thread: int) -> None:
+  """Tile width of the persistent kernels: 0 chooses per launch, 16 or 32
+  forces 4096- or 8192-element tiles where both kernels exist."""
+  rc = load().ascan_set_tile_width(int(elems_per_thread))
+  if rc != ASCAN_OK:
+    raise ValueError(f"tile width must be 0, 16 or 32, got {elems_per_thread}")
+
+
+def get_tile_width() -> int:
+  return int(load().ascan_get_tile_width())
 
 
 def get_implementation() -> str:

@@ -416,22 +416,22 @@ namespace ascan {
 // CTAs, 1 KB of each reserved by the hardware.
 constexpr size_t kSmemBudget = (228 * 1024) / tma::kCtasPerSm - 1024;
 
-template <typename T, int NIN, int NOUT, bool RG = false, int NS = 6>
+template <typename T, int NIN, int NOUT, int P, bool RG, int NS = 6>
 constexpr int ring_depth() {
   if constexpr (NS <= 2)
     return 2;
-  else if constexpr (tma::smem_bytes<NIN, NOUT, NS, T, RG>() <= kSmemBudget)
+  else if constexpr (tma::smem_bytes<NIN, NOUT, NS, T, P, RG>() <= kSmemBudget)
     return NS;
   else
-    return ring_depth<T, NIN, NOUT, RG, NS - 1>();
+    return ring_depth<T, NIN, NOUT, P, RG, NS - 1>();
 }
 
 // Whether the kernels that stage their outputs for TMA stores fit with a
 // two-stage ring; when they do not (large tiles), the register-store (RG)
 // kernels serve every schedule.
-template <typename T, int NIN, int NOUT>
+template <typename T, int NIN, int NOUT, int P>
 constexpr bool staged_fits() {
-  return tma::smem_bytes<NIN, NOUT, 2, T, false>() <= kSmemBudget;
+  return tma::smem_bytes<NIN, NOUT, 2, T, P, false>() <= kSmemBudget;
 }
 
 // Producer warp of both kernels: TMA loads and per-tile metadata.  Tickets
@@ -446,14 +446,17 @@ constexpr bool staged_fits() {
 // `Extra` fills the halo scalars and the ragged tail of one stage.
 // RG (ragged rows): tiles start anywhere inside a 128-byte TMA row; the box is
 // one TMA row taller and the tile's offset into it travels in the metadata.
-template <typename T, typename IdxT, bool REV, int NIN, int NOUT, int NS, bool RG, typename Extra>
-__device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, RG>& sm,
+template <typename T, typename IdxT, bool REV, int NIN, int NOUT, int NS, int P, bool RG,
+          typename Extra>
+__device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, P, RG>& sm,
                                              const CUtensorMap* const* maps,
                                              const tma::CuView<IdxT>& cu, int64_t N,
                                              int64_t n_tma_total, const tma::TileSched& sch,
                                              const TileStatus& st, int lane, Extra extra,
                                              int n_load = NIN) {
   using namespace tma;
+  constexpr int kTileElems = Geo<P>::kTileElems;
+  using F = Fmt<T, P>;
   if (lane == 0)
     for (int k = 0; k < NIN; ++k) prefetch_map(maps[k]);
   uint32_t stage = 0, phase = 0;
@@ -498,7 +501,7 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, RG>& sm
       break;
     }
     pending[stage] = false;  // its previous load was consumed and released
-    StageMeta<NIN, T>& m = sm.meta[stage];
+    StageMeta<NIN, T, P>& m = sm.meta[stage];
     if (ticket == kDone) {
       if (lane == 0) {
         m.ticket = kDone;
@@ -520,13 +523,13 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, RG>& sm
       t0 = t_flat;
       limit = N;
     }
-    const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow);
-    constexpr uint32_t kBoxBytes = (Fmt<T>::kRows + (RG ? 1 : 0)) * 128u;
+    const int row = static_cast<int>(p0 / F::kElemsPerRow);
+    constexpr uint32_t kBoxBytes = (F::kRows + (RG ? 1 : 0)) * 128u;
     const bool read_pred = sch.row_mode && ticket >= sch.stride;
     if (lane == 0) {
       m.ticket = ticket;
       if constexpr (RG)
-        m.shift = static_cast<uint32_t>(p0 - static_cast<int64_t>(row) * Fmt<T>::kElemsPerRow);
+        m.shift = static_cast<uint32_t>(p0 - static_cast<int64_t>(row) * F::kElemsPerRow);
       if (!read_pred) m.te_raw[1] = m.te_raw[3] = kStatusNone;
       // the first n_load inputs (an aggregate-only backward skips the states)
       mbar_expect_tx(&sm.full[stage], n_load * kBoxBytes + (read_pred ? 16u : 0u));
@@ -535,7 +538,7 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, RG>& sm
     }
     pending[stage] = true;
     last_parity[stage] = phase;
-    build_meta<IdxT, NIN, T>(m, cu, p0, t0, limit, n_tma_total, lane);
+    build_meta<IdxT, NIN, T, P>(m, cu, p0, t0, limit, n_tma_total, lane);
     const int64_t rem = limit - p0;
     const uint32_t n_valid = static_cast<uint32_t>(rem < kTileElems ? rem : kTileElems);
     int64_t nt = n_tma_total - p0;
@@ -569,15 +572,18 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, RG>& sm
 // separately so the ordinary kernels carry none of that code.
 // The CTA's part of one forward launch; the tensor maps are kernel
 // parameters (__grid_constant__), passed by address.
-template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO, bool RG>
+template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO, int P, bool RG>
 __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUtensorMap* map_x,
                                              const CUtensorMap* map_y,
                                              const CUtensorMap* map_gout,
                                              const FwdArgs<T, IdxT>& args, int64_t n_tma_total,
                                              const tma::TileSched& sch) {
   using namespace tma;
+  constexpr int kPerThread = P, kTileElems = Geo<P>::kTileElems, kBitWords = Geo<P>::kBitWords;
+  constexpr uint32_t kThreadMask = Geo<P>::kMask;
+  using F = Fmt<T, P>;
   constexpr int NIN = 2, NOUT = GATES_OUT ? 2 : 1;
-  using Sm = Smem<NIN, NOUT, NS, T, RG>;
+  using Sm = Smem<NIN, NOUT, NS, T, P, RG>;
   Sm& sm = smem_view<Sm>();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t S = args.S, BL = args.BL, N = args.N;
@@ -602,9 +608,9 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
 
   if (warp == kConsumerWarps) {
     const CUtensorMap* maps[NIN] = {map_g, map_x};
-    run_producer<T, IdxT, REV, NIN, NOUT, NS, RG>(
+    run_producer<T, IdxT, REV, NIN, NOUT, NS, P, RG>(
         sm, maps, cu, N, n_tma_total, sch, args.st, lane,
-        [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
+        [&](StageMeta<NIN, T, P>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
             uint64_t*) {
           for (uint32_t e = n_tma + ln; e < n_valid; e += 32) {
             m.tail[0][e - n_tma] = Cvt<T>::to(args.g[p0 + e]);
@@ -616,10 +622,10 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
 
   if (blockIdx.x == sch.cta0) validate_cu(args.cu, S, BL);
   const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
-  const ThreadChunks<T> tc(o);
+  const ThreadChunks<T, P> tc(o);
   const uint32_t bit_word = o >> 5, bit_shift = o & 31u;
-  constexpr int kPartRows = Fmt<T>::kRows / kConsumerWarps;    // this warp's slice of a tile
-  constexpr int kPartBytes = Fmt<T>::kBytes / kConsumerWarps;
+  constexpr int kPartRows = F::kRows / kConsumerWarps;    // this warp's slice of a tile
+  constexpr int kPartBytes = F::kBytes / kConsumerWarps;
   uint32_t stage = 0, phase = 0, obuf = 0, xi = 0;
   bool ok = true;
   while (true) {
@@ -631,7 +637,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
       ok = false;
       break;
     }
-    const StageMeta<NIN, T>& m = sm.meta[stage];
+    const StageMeta<NIN, T, P>& m = sm.meta[stage];
     const uint32_t ticket = m.ticket;
     if (ticket == kDone) break;
     const int64_t p0 = m.p0;
@@ -674,27 +680,27 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(a, b, head), lane, ex, wtot);
     if (early) take_early(early_raw, te_known, te_meta);
-    const Pfx P = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
+    const Pfx Pc = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
                                         sch.stride, te_known, te_meta, warp, lane, ok);
     // a, b hold the local prefixes: h = A_loc * carry + B_loc before the first head
-    const uint32_t cm = carry_mask<REV>(head);
-    if (IO && lastmask != 0u) record_row_agg<REV>(a, b, lastmask, cm, P, p0 + o, BL, args.io.agg);
+    const uint32_t cm = carry_mask<REV, P>(head);
+    if (IO && lastmask != 0u) record_row_agg<REV>(a, b, lastmask, cm, Pc, p0 + o, BL, args.io.agg);
     if (__all_sync(kFull, cm == kThreadMask)) {  // warp-uniform: no lane holds a head
 #pragma unroll
       for (int j = 0; j < kPerThread; ++j) {
-        b[j] = fmaf(a[j], P.b, b[j]);
-        if constexpr (GATES_OUT) a[j] *= P.a;
+        b[j] = fmaf(a[j], Pc.b, b[j]);
+        if constexpr (GATES_OUT) a[j] *= Pc.a;
       }
     } else {
 #pragma unroll
       for (int j = 0; j < kPerThread; ++j) {
         const bool c = (cm >> j) & 1u;
-        b[j] = c ? fmaf(a[j], P.b, b[j]) : b[j];
-        if constexpr (GATES_OUT) a[j] = c ? a[j] * P.a : a[j];
+        b[j] = c ? fmaf(a[j], Pc.b, b[j]) : b[j];
+        if constexpr (GATES_OUT) a[j] = c ? a[j] * Pc.a : a[j];
       }
     }
     const bool store = !IO || args.y != nullptr;  // false: aggregate-only pass
-    const uint32_t valid = below_mask(o, n_valid) & ~omask;
+    const uint32_t valid = below_mask<P>(o, n_valid) & ~omask;
     uint32_t direct = store ? valid : 0u;
     if (lane == 0) bulk_wait_read<1>();  // this warp's slice of staging buffer obuf is free
     __syncwarp();
@@ -705,7 +711,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     if constexpr (RG) {
       if (__all_sync(kFull, direct == kThreadMask)) {
         // ragged rows: a wholly valid warp slice leaves by realigned 16-byte stores
-        const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T>::kVec);
+        const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T, P>::kVec);
         store_realigned<T>(args.y, p0 + o, r, b, lane);
         if constexpr (GATES_OUT) store_realigned<T>(args.gout, p0 + o, r, a, lane);
         direct = 0u;
@@ -724,7 +730,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     __syncwarp();
     if (lane == 0) {
       if (slice_tma) {
-        const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow) + warp * kPartRows;
+        const int row = static_cast<int>(p0 / F::kElemsPerRow) + warp * kPartRows;
         tma_store_2d(map_y, 0, row, sm.out[obuf][0] + warp * kPartBytes);
         if constexpr (GATES_OUT) tma_store_2d(map_gout, 0, row, sm.out[obuf][1] + warp * kPartBytes);
       }
@@ -743,16 +749,19 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
 
 // The CTA's part of one backward launch (tensor maps passed by address, as
 // in fwd_tma_body).
-template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO, bool RG>
+template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO, int P, bool RG>
 __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CUtensorMap* map_g,
                                              const CUtensorMap* map_h, const CUtensorMap* map_dx,
                                              const CUtensorMap* map_dg,
                                              const BwdArgs<T, IdxT>& args, int64_t n_tma_total,
                                              const tma::TileSched& sch) {
   using namespace tma;
+  constexpr int kPerThread = P, kTileElems = Geo<P>::kTileElems, kBitWords = Geo<P>::kBitWords;
+  constexpr uint32_t kThreadMask = Geo<P>::kMask;
+  using F = Fmt<T, P>;
   constexpr bool REV = CAUSAL;
   constexpr int NIN = 3, NOUT = 2;
-  using Sm = Smem<NIN, NOUT, NS, T, RG>;
+  using Sm = Smem<NIN, NOUT, NS, T, P, RG>;
   Sm& sm = smem_view<Sm>();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t S = args.S, BL = args.BL, N = args.N;
@@ -777,9 +786,9 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
 
   if (warp == kConsumerWarps) {
     const CUtensorMap* maps[NIN] = {map_dy, map_g, map_h};
-    run_producer<T, IdxT, REV, NIN, NOUT, NS, RG>(
+    run_producer<T, IdxT, REV, NIN, NOUT, NS, P, RG>(
         sm, maps, cu, N, n_tma_total, sch, args.st, lane,
-        [&](StageMeta<NIN, T>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
+        [&](StageMeta<NIN, T, P>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
             uint64_t* bar) {
           for (uint32_t e = n_tma + ln; e < n_valid; e += 32) {
             m.tail[0][e - n_tma] = Cvt<T>::to(args.dy[p0 + e]);
@@ -832,10 +841,10 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
 
   if (blockIdx.x == sch.cta0) validate_cu(args.cu, S, BL);
   const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
-  const ThreadChunks<T> tc(o);
+  const ThreadChunks<T, P> tc(o);
   const uint32_t bit_word = o >> 5, bit_shift = o & 31u;
-  constexpr int kPartRows = Fmt<T>::kRows / kConsumerWarps;    // this warp's slice of a tile
-  constexpr int kPartBytes = Fmt<T>::kBytes / kConsumerWarps;
+  constexpr int kPartRows = F::kRows / kConsumerWarps;    // this warp's slice of a tile
+  constexpr int kPartBytes = F::kBytes / kConsumerWarps;
   uint32_t stage = 0, phase = 0, obuf = 0, xi = 0;
   bool ok = true;
   while (true) {
@@ -847,7 +856,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
       ok = false;
       break;
     }
-    const StageMeta<NIN, T>& m = sm.meta[stage];
+    const StageMeta<NIN, T, P>& m = sm.meta[stage];
     const uint32_t ticket = m.ticket;
     if (ticket == kDone) break;
     const int64_t p0 = m.p0;
@@ -938,19 +947,19 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(gv, dyv, head), lane, ex, wtot);
     if (early) take_early(early_raw, te_known, te_meta);
-    const Pfx P = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
+    const Pfx Pc = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
                                         sch.stride, te_known, te_meta, warp, lane, ok);
     // gv, dyv hold the local prefixes: dh = A_loc * carry + B_loc before the first head
-    const uint32_t cm = carry_mask<REV>(head);
-    if (IO && lastmask != 0u) record_row_agg<REV>(gv, dyv, lastmask, cm, P, p0 + o, BL, args.io.agg);
+    const uint32_t cm = carry_mask<REV, P>(head);
+    if (IO && lastmask != 0u) record_row_agg<REV>(gv, dyv, lastmask, cm, Pc, p0 + o, BL, args.io.agg);
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
-      const float d = ((cm >> j) & 1u) ? fmaf(gv[j], P.b, dyv[j]) : dyv[j];
+      const float d = ((cm >> j) & 1u) ? fmaf(gv[j], Pc.b, dyv[j]) : dyv[j];
       dyv[j] = d;                                    // dx
       gv[j] = ((tail >> j) & 1u) ? 0.f : d * hv[j];  // dg
     }
     const bool store = !IO || args.dx != nullptr;  // false: aggregate-only pass
-    const uint32_t valid = below_mask(o, n_valid) & ~omask;
+    const uint32_t valid = below_mask<P>(o, n_valid) & ~omask;
     uint32_t direct = store ? valid : 0u;
     if (lane == 0) bulk_wait_read<1>();  // this warp's slice of staging buffer obuf is free
     __syncwarp();
@@ -961,7 +970,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     if constexpr (RG) {
       if (__all_sync(kFull, direct == kThreadMask)) {
         // ragged rows: a wholly valid warp slice leaves by realigned 16-byte stores
-        const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T>::kVec);
+        const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T, P>::kVec);
         store_realigned<T>(args.dx, p0 + o, r, dyv, lane);
         store_realigned<T>(args.dg, p0 + o, r, gv, lane);
         direct = 0u;
@@ -980,7 +989,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     __syncwarp();
     if (lane == 0) {
       if (slice_tma) {
-        const int row = static_cast<int>(p0 / Fmt<T>::kElemsPerRow) + warp * kPartRows;
+        const int row = static_cast<int>(p0 / F::kElemsPerRow) + warp * kPartRows;
         tma_store_2d(map_dx, 0, row, sm.out[obuf][0] + warp * kPartBytes);
         tma_store_2d(map_dg, 0, row, sm.out[obuf][1] + warp * kPartBytes);
       }
@@ -997,18 +1006,18 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
   if (lane == 0) bulk_wait_all();
 }
 
-template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO, bool RG>
+template <typename T, typename IdxT, bool REV, bool GATES_OUT, int NS, bool IO, int P, bool RG>
 __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     scan_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_g,
                         const __grid_constant__ CUtensorMap map_x,
                         const __grid_constant__ CUtensorMap map_y,
                         const __grid_constant__ CUtensorMap map_gout, const FwdArgs<T, IdxT> args,
                         int64_t n_tma_total, const tma::TileSched sch) {
-  fwd_tma_body<T, IdxT, REV, GATES_OUT, NS, IO, RG>(&map_g, &map_x, &map_y, &map_gout, args,
+  fwd_tma_body<T, IdxT, REV, GATES_OUT, NS, IO, P, RG>(&map_g, &map_x, &map_y, &map_gout, args,
                                                     n_tma_total, sch);
 }
 
-template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO, bool RG>
+template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO, int P, bool RG>
 __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     scan_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dy,
                         const __grid_constant__ CUtensorMap map_g,
@@ -1016,7 +1025,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
                         const __grid_constant__ CUtensorMap map_dx,
                         const __grid_constant__ CUtensorMap map_dg, const BwdArgs<T, IdxT> args,
                         int64_t n_tma_total, const tma::TileSched sch) {
-  bwd_tma_body<T, IdxT, CAUSAL, NS, IO, RG>(&map_dy, &map_g, &map_h, &map_dx, &map_dg, args,
+  bwd_tma_body<T, IdxT, CAUSAL, NS, IO, P, RG>(&map_dy, &map_g, &map_h, &map_dx, &map_dg, args,
                                             n_tma_total, sch);
 }
 
@@ -1026,7 +1035,7 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
 // tickets, status slots and abort words); the launch is cooperative, so both
 // groups are resident and each moves through its own tickets as a separate
 // launch would.
-template <typename T, typename IdxT, int NS, bool RG>
+template <typename T, typename IdxT, int NS, int P, bool RG>
 __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     scan_fwd_bidi_tma_kernel(const __grid_constant__ CUtensorMap f_g,
                              const __grid_constant__ CUtensorMap f_x,
@@ -1037,14 +1046,14 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
                              const FwdArgs<T, IdxT> ba, int64_t n_tma_total,
                              const tma::TileSched fs, const tma::TileSched bs) {
   if (blockIdx.x < bs.cta0)
-    fwd_tma_body<T, IdxT, false, false, NS, false, RG>(&f_g, &f_x, &f_y, &f_y, fa, n_tma_total, fs);
+    fwd_tma_body<T, IdxT, false, false, NS, false, P, RG>(&f_g, &f_x, &f_y, &f_y, fa, n_tma_total, fs);
   else
-    fwd_tma_body<T, IdxT, true, false, NS, false, RG>(&b_g, &b_x, &b_y, &b_y, ba, n_tma_total, bs);
+    fwd_tma_body<T, IdxT, true, false, NS, false, P, RG>(&b_g, &b_x, &b_y, &b_y, ba, n_tma_total, bs);
 }
 
 // Adjoint of scan_fwd_bidi_tma_kernel: the causal adjoint on CTAs [0, bs.cta0),
 // the reverse adjoint on the others.
-template <typename T, typename IdxT, int NS, bool RG>
+template <typename T, typename IdxT, int NS, int P, bool RG>
 __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
     scan_bwd_bidi_tma_kernel(const __grid_constant__ CUtensorMap f_dy,
                              const __grid_constant__ CUtensorMap f_g,
@@ -1059,9 +1068,9 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
                              const BwdArgs<T, IdxT> ba, int64_t n_tma_total,
                              const tma::TileSched fs, const tma::TileSched bs) {
   if (blockIdx.x < bs.cta0)
-    bwd_tma_body<T, IdxT, true, NS, false, RG>(&f_dy, &f_g, &f_h, &f_dx, &f_dg, fa, n_tma_total, fs);
+    bwd_tma_body<T, IdxT, true, NS, false, P, RG>(&f_dy, &f_g, &f_h, &f_dx, &f_dg, fa, n_tma_total, fs);
   else
-    bwd_tma_body<T, IdxT, false, NS, false, RG>(&b_dy, &b_g, &b_h, &b_dx, &b_dg, ba, n_tma_total,
+    bwd_tma_body<T, IdxT, false, NS, false, P, RG>(&b_dy, &b_g, &b_h, &b_dx, &b_dg, ba, n_tma_total,
                                                 bs);
 }
 
@@ -1157,20 +1166,20 @@ struct Workspace {
 };
 
 // Tiles of the plain kernels (kTile elements) and of the persistent TMA
-// kernels (tma::kTileElems; one divides the other); status slots are counted
-// in the smaller tiles so that either family fits the same workspace.
+// kernels (4096 or 8192 elements; one divides the other); status slots are
+// counted in the smallest tiles so that every kernel fits the same workspace.
 static size_t tiles_of(int64_t n) { return static_cast<size_t>((n + kTile - 1) / kTile); }
 static size_t tma_tiles_of(int64_t n) {
-  return static_cast<size_t>((n + tma::kTileElems - 1) / tma::kTileElems);
+  return static_cast<size_t>((n + tma::kMinTileElems - 1) / tma::kMinTileElems);
 }
 // Row order with ragged rows (BL not a multiple of the tile) cuts every row
 // into ceil(BL / tile) tiles, a few more than the flat count.
 static size_t status_slots(int64_t C, int64_t BL, bool ragged) {
   const size_t plain = tiles_of(C * BL), tma_flat = tma_tiles_of(C * BL);
   const size_t flat = plain > tma_flat ? plain : tma_flat;  // either kernel family
-  if (!ragged || BL < tma::kTileElems) return flat;  // ragged rows are at least a tile
+  if (!ragged || BL < tma::kMinTileElems) return flat;  // ragged rows are at least a tile
   const size_t rows = static_cast<size_t>(C) *
-                      static_cast<size_t>((BL + tma::kTileElems - 1) / tma::kTileElems);
+                      static_cast<size_t>((BL + tma::kMinTileElems - 1) / tma::kMinTileElems);
   return rows > flat ? rows : flat;
 }
 
@@ -1377,12 +1386,11 @@ static bool split_bidi(int cap, tma::TileSched& fs, tma::TileSched& bs, uint32_t
 // allow_ragged: rows that are not whole tiles may be cut into whole tiles and
 // a partial last one (the workspace has their status slots and the launch
 // has no slab I/O).
-static tma::TileSched make_sched(uint32_t num_tiles, int64_t N, int64_t BL, int64_t S,
+static tma::TileSched make_sched(int64_t kT, int64_t N, int64_t BL, int64_t S,
                                  bool allow_ragged) {
-  tma::TileSched sch{num_tiles, 0u, 0u, 0u, 1u, 0u, 0u, 0u};
+  tma::TileSched sch{static_cast<uint32_t>((N + kT - 1) / kT), 0u, 0u, 0u, 1u, 0u, 0u, 0u};
   const int64_t C = BL > 0 ? N / BL : 0;
   const int mode = impl_mode();
-  constexpr int64_t kT = tma::kTileElems;
   const int64_t per_row = BL > 0 ? (BL + kT - 1) / kT : 0;
   const bool aligned = BL % kT == 0;
   const bool fits = BL >= kT && C >= 1 && C <= 0x7fffffffll && C * per_row <= 0xffffffffll &&
@@ -1400,18 +1408,43 @@ static tma::TileSched make_sched(uint32_t num_tiles, int64_t N, int64_t BL, int6
   return sch;
 }
 
+// ---- tile width -----------------------------------------------------------
+
+// 0: automatic; 16 or 32: elements per consumer thread forced wherever both
+// kernels exist (tests and tuning; ascan_set_tile_width).
+static int g_tile_width = 0;
+
+// Whether a launch runs 8192-element tiles (32 elements per thread) rather
+// than 4096-element ones.  Wide tiles halve the consumer warps' fixed
+// per-tile chain (fold, warp scan, hand-offs, carry) per byte: measured on
+// B200 the fp32 forward at B=8, C=1536 goes from 143 to 106 us (T=4096) and
+// from 2264 to 1483 us (T=65536), and the fp16 forward and backward at
+// T=2048 from 76/92 to 55/69 us.  They lose when rows are few (each row's
+// tiles form a serial chain: C=257, T=100003 went from 119 to 204 us), when
+// there are too few tiles to fill the SMs, and in ragged forward rows.
+static bool use_wide(int64_t N, int64_t BL, int64_t S, bool allow_ragged, bool ragged_ok) {
+  if (g_tile_width != 0) return g_tile_width == 32;
+  const tma::TileSched sch = make_sched(tma::Geo<32>::kTileElems, N, BL, S, allow_ragged);
+  if (sch.ragged && !ragged_ok) return false;
+  const uint32_t sms = static_cast<uint32_t>(sm_count());
+  if (sms == 0 || sch.num_tiles < 2 * sms) return false;
+  if (sch.row_mode && sch.rows < 4 * sms) return false;
+  return true;
+}
+
 // 1: launched, 0: not applicable (caller falls back to the plain kernel), <0: error
-template <typename T, typename IdxT, bool REV, bool GOUT, bool RG>
+template <typename T, typename IdxT, bool REV, bool GOUT, int P, bool RG>
 static int launch_fwd_tma_sched(const FwdArgs<T, IdxT>& a, const tma::TileSched& sch0, bool io,
                                 cudaStream_t s) {
+  using F = tma::Fmt<T, P>;
   constexpr int NOUT = GOUT ? 2 : 1;
-  constexpr int NS = ring_depth<T, 2, NOUT, RG>();
-  constexpr size_t smem = tma::smem_bytes<2, NOUT, NS, T, RG>();
+  constexpr int NS = ring_depth<T, 2, NOUT, P, RG>();
+  constexpr size_t smem = tma::smem_bytes<2, NOUT, NS, T, P, RG>();
   static_assert(smem <= kSmemBudget, "TMA forward ring does not fit in shared memory");
-  const int64_t rows = a.N / tma::Fmt<T>::kElemsPerRow;
+  const int64_t rows = a.N / F::kElemsPerRow;
   CUtensorMap mg, mx, my, mgo;
-  constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;  // stores: one warp's slice
-  constexpr int kInRows = tma::Fmt<T>::kRows + (RG ? 1 : 0);     // ragged: one more row
+  constexpr int kPart = F::kRows / tma::kConsumerWarps;  // stores: one warp's slice
+  constexpr int kInRows = F::kRows + (RG ? 1 : 0);     // ragged: one more row
   // an aggregate-only pass stores nothing: its output map is a never-used view of g
   if (!make_map<T>(&mg, a.g, rows, kInRows) || !make_map<T>(&mx, a.x, rows, kInRows) ||
       !make_map<T>(&my, a.y ? a.y : a.g, rows, kPart))
@@ -1422,12 +1455,12 @@ static int launch_fwd_tma_sched(const FwdArgs<T, IdxT>& a, const tma::TileSched&
     mgo = my;
   }
   const void* kern;
-  if constexpr (RG)
-    kern = reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false, true>);
+  if constexpr (RG || P != 16)  // slab I/O: staged 4096-element kernels only
+    kern = reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false, P, RG>);
   else
-    kern = io ? reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, true, false>)
-              : reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false, false>);
-  int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
+    kern = io ? reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, true, P, false>)
+              : reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false, P, false>);
+  int64_t n_tma_total = rows * F::kElemsPerRow;
   FwdArgs<T, IdxT> b = a;
   tma::TileSched sch = sch0;
   b.num_tiles = sch.num_tiles;
@@ -1435,45 +1468,57 @@ static int launch_fwd_tma_sched(const FwdArgs<T, IdxT>& a, const tma::TileSched&
   return launch_cooperative(kern, smem, b.num_tiles, params, s);
 }
 
+template <typename T, typename IdxT, bool REV, bool GOUT, int P>
+static int launch_fwd_tma_p(const FwdArgs<T, IdxT>& a, bool allow_ragged, bool io,
+                            cudaStream_t s) {
+  // ragged rows need the shifted-tile kernels, which exist without slab I/O only
+  const tma::TileSched sch =
+      make_sched(tma::Geo<P>::kTileElems, a.N, a.BL, a.S, allow_ragged && !io);
+  constexpr bool kStaged = staged_fits<T, 2, GOUT ? 2 : 1, P>();
+  if (sch.ragged || !kStaged) {
+    if (io) return 0;  // slab I/O exists in the staged kernels only
+    return launch_fwd_tma_sched<T, IdxT, REV, GOUT, P, true>(a, sch, io, s);
+  }
+  if constexpr (kStaged) return launch_fwd_tma_sched<T, IdxT, REV, GOUT, P, false>(a, sch, io, s);
+  return 0;
+}
+
 // allow_ragged is passed beside the kernel arguments, not inside them: the
 // argument structs are what the kernels receive.
 template <typename T, typename IdxT, bool REV, bool GOUT>
 static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, bool allow_ragged, cudaStream_t s) {
   const bool io = a.io.carry || a.io.halo || a.io.agg || !a.y;
-  // ragged rows need the shifted-tile kernels, which exist without slab I/O only
-  const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(a.N)), a.N, a.BL,
-                                        a.S, allow_ragged && !io);
-  constexpr bool kStaged = staged_fits<T, 2, GOUT ? 2 : 1>();
-  if (sch.ragged || !kStaged) {
-    if (io) return 0;  // slab I/O exists in the staged kernels only
-    return launch_fwd_tma_sched<T, IdxT, REV, GOUT, true>(a, sch, io, s);
+  // wide tiles for the plain forward (the gate-product output stays narrow)
+  if constexpr (!GOUT) {
+    if (!io && use_wide(a.N, a.BL, a.S, allow_ragged, false))
+      return launch_fwd_tma_p<T, IdxT, REV, GOUT, 32>(a, allow_ragged, io, s);
   }
-  if constexpr (kStaged) return launch_fwd_tma_sched<T, IdxT, REV, GOUT, false>(a, sch, io, s);
-  return 0;
+  return launch_fwd_tma_p<T, IdxT, REV, GOUT, 16>(a, allow_ragged, io, s);
 }
 
-template <typename T, typename IdxT, bool CAUSAL, bool RG>
+template <typename T, typename IdxT, bool CAUSAL, int P, bool RG>
 static int launch_bwd_tma_sched(const BwdArgs<T, IdxT>& a, const tma::TileSched& sch0, bool io,
                                 cudaStream_t s) {
-  constexpr int NS = ring_depth<T, 3, 2, RG>();
-  constexpr size_t smem = tma::smem_bytes<3, 2, NS, T, RG>();
+  using F = tma::Fmt<T, P>;
+  constexpr int NS = ring_depth<T, 3, 2, P, RG>();
+  constexpr size_t smem = tma::smem_bytes<3, 2, NS, T, P, RG>();
   static_assert(smem <= kSmemBudget, "TMA backward ring does not fit in shared memory");
-  const int64_t rows = a.N / tma::Fmt<T>::kElemsPerRow;
+  const int64_t rows = a.N / F::kElemsPerRow;
   CUtensorMap mdy, mg, mh, mdx, mdg;
-  constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;  // stores: one warp's slice
-  constexpr int kInRows = tma::Fmt<T>::kRows + (RG ? 1 : 0);     // ragged: one more row
+  constexpr int kPart = F::kRows / tma::kConsumerWarps;  // stores: one warp's slice
+  constexpr int kInRows = F::kRows + (RG ? 1 : 0);     // ragged: one more row
   if (!make_map<T>(&mdy, a.dy, rows, kInRows) || !make_map<T>(&mg, a.g, rows, kInRows) ||
       !make_map<T>(&mh, a.h, rows, kInRows) ||
       !make_map<T>(&mdx, a.dx ? a.dx : a.dy, rows, kPart) ||
       !make_map<T>(&mdg, a.dg ? a.dg : a.dy, rows, kPart))
     return 0;
   const void* kern;
-  if constexpr (RG)
-    kern = reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false, true>);
+  if constexpr (RG || P != 16)
+    kern = reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false, P, RG>);
   else
-    kern = io ? reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, true, false>)
-              : reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false, false>);
-  int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
+    kern = io ? reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, true, P, false>)
+              : reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false, P, false>);
+  int64_t n_tma_total = rows * F::kElemsPerRow;
   BwdArgs<T, IdxT> b = a;
   tma::TileSched sch = sch0;
   b.num_tiles = sch.num_tiles;
@@ -1481,18 +1526,34 @@ static int launch_bwd_tma_sched(const BwdArgs<T, IdxT>& a, const tma::TileSched&
   return launch_cooperative(kern, smem, b.num_tiles, params, s);
 }
 
+template <typename T, typename IdxT, bool CAUSAL, int P>
+static int launch_bwd_tma_p(const BwdArgs<T, IdxT>& a, bool allow_ragged, bool io,
+                            cudaStream_t s) {
+  const tma::TileSched sch =
+      make_sched(tma::Geo<P>::kTileElems, a.N, a.BL, a.S, allow_ragged && !io);
+  constexpr bool kStaged = staged_fits<T, 3, 2, P>();
+  if (sch.ragged || !kStaged) {
+    if (io) return 0;  // slab I/O exists in the staged kernels only
+    return launch_bwd_tma_sched<T, IdxT, CAUSAL, P, true>(a, sch, io, s);
+  }
+  if constexpr (kStaged) return launch_bwd_tma_sched<T, IdxT, CAUSAL, P, false>(a, sch, io, s);
+  return 0;
+}
+
+// 16-bit types take wide tiles in the backward too (the same bytes per tile
+// as fp32 at 16 elements per thread); fp32 keeps 4096-element tiles, whose
+// three inputs and two staged outputs fill the shared memory.
+template <typename T>
+constexpr bool kWideBwd = sizeof(T) == 2;
+
 template <typename T, typename IdxT, bool CAUSAL>
 static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, bool allow_ragged, cudaStream_t s) {
   const bool io = a.io.carry || a.io.halo || a.io.agg || !a.dx;
-  const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(a.N)), a.N, a.BL,
-                                        a.S, allow_ragged && !io);
-  constexpr bool kStaged = staged_fits<T, 3, 2>();
-  if (sch.ragged || !kStaged) {
-    if (io) return 0;  // slab I/O exists in the staged kernels only
-    return launch_bwd_tma_sched<T, IdxT, CAUSAL, true>(a, sch, io, s);
+  if constexpr (kWideBwd<T>) {
+    if (!io && use_wide(a.N, a.BL, a.S, allow_ragged, true))
+      return launch_bwd_tma_p<T, IdxT, CAUSAL, 32>(a, allow_ragged, io, s);
   }
-  if constexpr (kStaged) return launch_bwd_tma_sched<T, IdxT, CAUSAL, false>(a, sch, io, s);
-  return 0;
+  return launch_bwd_tma_p<T, IdxT, CAUSAL, 16>(a, allow_ragged, io, s);
 }
 
 template <typename T, typename IdxT, int VEC>
@@ -1609,26 +1670,26 @@ static int bwd_typed(const void* dy, const void* g, const void* h, void* dx, voi
 // One cooperative launch for the two scans of a bidirectional pair (same
 // geometry and cu_seqlens, independent data).  1: launched, 0: not possible
 // here (the caller runs the two scans one after the other), <0: error.
-template <typename T, typename IdxT, bool RG>
+template <typename T, typename IdxT, int P, bool RG>
 static int launch_fwd_bidi_sched(const FwdArgs<T, IdxT>& fa, const FwdArgs<T, IdxT>& ba,
                                  tma::TileSched fs, tma::TileSched bs, cudaStream_t s) {
-  constexpr int NS = ring_depth<T, 2, 1, RG>();
-  constexpr size_t smem = tma::smem_bytes<2, 1, NS, T, RG>();
+  constexpr int NS = ring_depth<T, 2, 1, P, RG>();
+  constexpr size_t smem = tma::smem_bytes<2, 1, NS, T, P, RG>();
   static_assert(smem <= kSmemBudget, "TMA forward ring does not fit in shared memory");
-  const int64_t rows = fa.N / tma::Fmt<T>::kElemsPerRow;
-  constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;
-  constexpr int kInRows = tma::Fmt<T>::kRows + (RG ? 1 : 0);
+  const int64_t rows = fa.N / tma::Fmt<T, P>::kElemsPerRow;
+  constexpr int kPart = tma::Fmt<T, P>::kRows / tma::kConsumerWarps;
+  constexpr int kInRows = tma::Fmt<T, P>::kRows + (RG ? 1 : 0);
   CUtensorMap fg, fx, fy, bg, bx, by;
   if (!make_map<T>(&fg, fa.g, rows, kInRows) || !make_map<T>(&fx, fa.x, rows, kInRows) ||
       !make_map<T>(&fy, fa.y, rows, kPart) || !make_map<T>(&bg, ba.g, rows, kInRows) ||
       !make_map<T>(&bx, ba.x, rows, kInRows) || !make_map<T>(&by, ba.y, rows, kPart))
     return 0;
-  const void* kern = reinterpret_cast<const void*>(scan_fwd_bidi_tma_kernel<T, IdxT, NS, RG>);
+  const void* kern = reinterpret_cast<const void*>(scan_fwd_bidi_tma_kernel<T, IdxT, NS, P, RG>);
   const int cap = coop_capacity(kern, smem);
   if (cap <= 0) return cap;
   uint32_t grid = 0;
   if (!split_bidi(cap, fs, bs, grid)) return 0;
-  int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
+  int64_t n_tma_total = rows * tma::Fmt<T, P>::kElemsPerRow;
   FwdArgs<T, IdxT> f = fa, b = ba;
   f.num_tiles = fs.num_tiles;
   b.num_tiles = bs.num_tiles;
@@ -1636,15 +1697,15 @@ static int launch_fwd_bidi_sched(const FwdArgs<T, IdxT>& fa, const FwdArgs<T, Id
   return launch_coop_grid(kern, smem, grid, params, s);
 }
 
-template <typename T, typename IdxT, bool RG>
+template <typename T, typename IdxT, int P, bool RG>
 static int launch_bwd_bidi_sched(const BwdArgs<T, IdxT>& fa, const BwdArgs<T, IdxT>& ba,
                                  tma::TileSched fs, tma::TileSched bs, cudaStream_t s) {
-  constexpr int NS = ring_depth<T, 3, 2, RG>();
-  constexpr size_t smem = tma::smem_bytes<3, 2, NS, T, RG>();
+  constexpr int NS = ring_depth<T, 3, 2, P, RG>();
+  constexpr size_t smem = tma::smem_bytes<3, 2, NS, T, P, RG>();
   static_assert(smem <= kSmemBudget, "TMA backward ring does not fit in shared memory");
-  const int64_t rows = fa.N / tma::Fmt<T>::kElemsPerRow;
-  constexpr int kPart = tma::Fmt<T>::kRows / tma::kConsumerWarps;
-  constexpr int kInRows = tma::Fmt<T>::kRows + (RG ? 1 : 0);
+  const int64_t rows = fa.N / tma::Fmt<T, P>::kElemsPerRow;
+  constexpr int kPart = tma::Fmt<T, P>::kRows / tma::kConsumerWarps;
+  constexpr int kInRows = tma::Fmt<T, P>::kRows + (RG ? 1 : 0);
   CUtensorMap m[10];
   const BwdArgs<T, IdxT>* both[2] = {&fa, &ba};
   for (int d = 0; d < 2; ++d) {
@@ -1655,18 +1716,39 @@ static int launch_bwd_bidi_sched(const BwdArgs<T, IdxT>& fa, const BwdArgs<T, Id
         !make_map<T>(&md[4], a.dg, rows, kPart))
       return 0;
   }
-  const void* kern = reinterpret_cast<const void*>(scan_bwd_bidi_tma_kernel<T, IdxT, NS, RG>);
+  const void* kern = reinterpret_cast<const void*>(scan_bwd_bidi_tma_kernel<T, IdxT, NS, P, RG>);
   const int cap = coop_capacity(kern, smem);
   if (cap <= 0) return cap;
   uint32_t grid = 0;
   if (!split_bidi(cap, fs, bs, grid)) return 0;
-  int64_t n_tma_total = rows * tma::Fmt<T>::kElemsPerRow;
+  int64_t n_tma_total = rows * tma::Fmt<T, P>::kElemsPerRow;
   BwdArgs<T, IdxT> f = fa, b = ba;
   f.num_tiles = fs.num_tiles;
   b.num_tiles = bs.num_tiles;
   void* params[] = {&m[0], &m[1], &m[2], &m[3], &m[4], &m[5], &m[6], &m[7], &m[8], &m[9],
                     &f,    &b,    &n_tma_total, &fs, &bs};
   return launch_coop_grid(kern, smem, grid, params, s);
+}
+
+// Tile order and kernel variant of a bidirectional launch at tile width P.
+template <typename T, typename IdxT, int P>
+static int launch_fwd_bidi_p(const FwdArgs<T, IdxT>& fa, const FwdArgs<T, IdxT>& ba,
+                             bool allow_ragged, cudaStream_t s) {
+  const tma::TileSched sch = make_sched(tma::Geo<P>::kTileElems, fa.N, fa.BL, fa.S, allow_ragged);
+  if constexpr (staged_fits<T, 2, 1, P>()) {
+    if (!sch.ragged) return launch_fwd_bidi_sched<T, IdxT, P, false>(fa, ba, sch, sch, s);
+  }
+  return launch_fwd_bidi_sched<T, IdxT, P, true>(fa, ba, sch, sch, s);
+}
+
+template <typename T, typename IdxT, int P>
+static int launch_bwd_bidi_p(const BwdArgs<T, IdxT>& fa, const BwdArgs<T, IdxT>& ba,
+                             bool allow_ragged, cudaStream_t s) {
+  const tma::TileSched sch = make_sched(tma::Geo<P>::kTileElems, fa.N, fa.BL, fa.S, allow_ragged);
+  if constexpr (staged_fits<T, 3, 2, P>()) {
+    if (!sch.ragged) return launch_bwd_bidi_sched<T, IdxT, P, false>(fa, ba, sch, sch, s);
+  }
+  return launch_bwd_bidi_sched<T, IdxT, P, true>(fa, ba, sch, sch, s);
 }
 
 // Causal scan of (gf, xf) and reverse scan of (gb, xb): one launch when the
@@ -1698,14 +1780,10 @@ static int fwd_bidi_typed(const void* gf, const void* xf, void* yf, const void* 
       a.st = ws[d]->st;
       a.io = RowIO{nullptr, nullptr, nullptr};
     }
-    const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(N)), N, BL, S,
-                                          wf.allow_ragged && wb.allow_ragged);
-    int rc = 0;
-    if constexpr (staged_fits<T, 2, 1>())
-      rc = sch.ragged ? launch_fwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s)
-                      : launch_fwd_bidi_sched<T, IdxT, false>(fa, ba, sch, sch, s);
-    else
-      rc = launch_fwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s);
+    const bool ragged_ok = wf.allow_ragged && wb.allow_ragged;
+    const int rc = use_wide(N, BL, S, ragged_ok, false)
+                       ? launch_fwd_bidi_p<T, IdxT, 32>(fa, ba, ragged_ok, s)
+                       : launch_fwd_bidi_p<T, IdxT, 16>(fa, ba, ragged_ok, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
   }
   const int rc = fwd_typed<T, IdxT>(gf, xf, yf, nullptr, cu, S, C, BL, 0, wf, s);
@@ -1743,14 +1821,14 @@ static int bwd_bidi_typed(const void* const (&in)[2][3], void* const (&out)[2][2
       a.st = ws[d]->st;
       a.io = RowIO{nullptr, nullptr, nullptr};
     }
-    const tma::TileSched sch = make_sched(static_cast<uint32_t>(tma_tiles_of(N)), N, BL, S,
-                                          wf.allow_ragged && wb.allow_ragged);
-    int rc = 0;
-    if constexpr (staged_fits<T, 3, 2>())
-      rc = sch.ragged ? launch_bwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s)
-                      : launch_bwd_bidi_sched<T, IdxT, false>(fa, ba, sch, sch, s);
+    const bool ragged_ok = wf.allow_ragged && wb.allow_ragged;
+    int rc;
+    if constexpr (kWideBwd<T>)
+      rc = use_wide(N, BL, S, ragged_ok, true)
+               ? launch_bwd_bidi_p<T, IdxT, 32>(fa, ba, ragged_ok, s)
+               : launch_bwd_bidi_p<T, IdxT, 16>(fa, ba, ragged_ok, s);
     else
-      rc = launch_bwd_bidi_sched<T, IdxT, true>(fa, ba, sch, sch, s);
+      rc = launch_bwd_bidi_p<T, IdxT, 16>(fa, ba, ragged_ok, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
   }
   const int rc = bwd_typed<T, IdxT>(in[0][0], in[0][1], in[0][2], out[0][0], out[0][1], cu, S, C,
@@ -2096,6 +2174,15 @@ int ascan_set_implementation(int impl) {
 }
 
 int ascan_get_implementation(void) { return impl_mode(); }
+
+int ascan_set_tile_width(int elems_per_thread) {
+  if (elems_per_thread != 0 && elems_per_thread != 16 && elems_per_thread != 32)
+    return ASCAN_EINVAL;
+  g_tile_width = elems_per_thread;
+  return ASCAN_OK;
+}
+
+int ascan_get_tile_width(void) { return g_tile_width; }
 
 int ascan_get_device_error(int device, unsigned int* code, long long* detail) {
   int prev = -1;

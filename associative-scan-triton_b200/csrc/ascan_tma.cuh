@@ -43,29 +43,31 @@ constexpr int kCtasPerSm = 32 / kConsumerWarps / 4;       // 2 for 4 warps, 1 fo
 static_assert(kCtasPerSm >= 1, "4 or 8 consumer warps");
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;        // + producer warp
-// Elements per consumer thread (compile-time): 16 by default; 32 doubles the
-// tile (8192 elements with 8 warps), halving the per-tile fixed costs per
-// byte at the price of shared memory (two stages, and kernels whose staged
-// outputs no longer fit store them from registers).
-#ifndef ASCAN_PER_THREAD
-#define ASCAN_PER_THREAD 16
-#endif
-constexpr int kPerThread = ASCAN_PER_THREAD;
-static_assert(kPerThread == 16 || kPerThread == 32, "16 or 32 elements per thread");
-// bits of one thread's elements in a 32-bit mask
-constexpr uint32_t kThreadMask = kPerThread == 32 ? 0xffffffffu : (1u << kPerThread) - 1u;
-constexpr int kTileElems = kConsumers * kPerThread;  // 4096 (8 warps x 16)
-static_assert(kTile % kTileElems == 0 || kTileElems % kTile == 0,
+// Tile geometry per kernel: P elements per consumer thread (16 or 32), so a
+// tile holds 256 P elements (8 consumer warps).  P = 32 halves the per-tile
+// fixed costs per byte (the consumer warps run one dependent chain per tile)
+// at the price of shared memory and registers; the launcher picks P per
+// kernel and dtype.
+template <int P>
+struct Geo {
+  static_assert(P == 16 || P == 32, "16 or 32 elements per thread");
+  static constexpr int kPerThread = P;
+  static constexpr uint32_t kMask = P == 32 ? 0xffffffffu : (1u << (P % 32)) - 1u;
+  static constexpr int kTileElems = kConsumers * P;
+  static constexpr int kBitWords = kTileElems / 32;
+};
+// The smallest TMA tile: status slots are counted in it.
+constexpr int kMinTileElems = Geo<16>::kTileElems;
+static_assert(kTile % kMinTileElems == 0 || kMinTileElems % kTile == 0,
               "TMA tiles and the plain kernels' tiles nest (status slots count the smaller)");
-constexpr int kBitWords = kTileElems / 32;
 constexpr int kCuCache = 1024;                   // cu_seqlens entries cached in smem
 constexpr uint32_t kDone = 0xffffffffu;
 
-template <typename T>
+template <typename T, int P = 16>
 struct Fmt {
   static constexpr int kElemsPerRow = 128 / sizeof(T);  // one 128-byte TMA row
-  static constexpr int kRows = kTileElems / kElemsPerRow;
-  static constexpr int kBytes = kTileElems * sizeof(T);
+  static constexpr int kRows = Geo<P>::kTileElems / kElemsPerRow;
+  static constexpr int kBytes = Geo<P>::kTileElems * sizeof(T);
   static constexpr int kTailMax = kElemsPerRow;         // ragged tail < one row
 };
 
@@ -183,7 +185,7 @@ __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
 // shared-memory layout
 // ---------------------------------------------------------------------------
 
-template <int NIN, typename T>
+template <int NIN, typename T, int P>
 struct StageMeta {
   uint32_t ticket;     // kDone: no more tiles
   uint32_t n_valid;    // tile elements below N
@@ -202,9 +204,9 @@ struct StageMeta {
   // copy together with the tile (all zero = unknown); an inclusive record in
   // it is the tile's carry-in
   alignas(16) uint32_t te_raw[4];
-  alignas(16) uint32_t sbits[kBitWords];  // sequence starts (and positions outside any sequence)
-  alignas(16) uint32_t ebits[kBitWords];  // sequence ends   (and positions outside any sequence)
-  alignas(16) uint32_t obits[kBitWords];  // positions outside any sequence (valid if has_outside)
+  alignas(16) uint32_t sbits[Geo<P>::kBitWords];  // sequence starts (and positions outside any sequence)
+  alignas(16) uint32_t ebits[Geo<P>::kBitWords];  // sequence ends   (and positions outside any sequence)
+  alignas(16) uint32_t obits[Geo<P>::kBitWords];  // positions outside any sequence (valid if has_outside)
   float tail[NIN][Fmt<T>::kTailMax];
 };
 
@@ -219,7 +221,7 @@ struct TileSched {
   uint32_t num_tiles;
   uint32_t row_mode;
   uint32_t rows;            // row mode: C
-  uint32_t tiles_per_row;   // row mode: ceil(BL / kTileElems)
+  uint32_t tiles_per_row;   // row mode: ceil(BL / tile elements)
   uint32_t stride;          // ticket distance to the scan predecessor
   uint32_t ragged;          // row mode with BL not a multiple of the tile (last tile of a row partial)
   uint32_t cta0;            // first CTA of this scan's group (0 unless bidirectional)
@@ -241,17 +243,17 @@ struct XSlot {
 // RG (ragged rows): a tile may start anywhere inside a 128-byte TMA row, so
 // each input buffer holds one more TMA row (padded to the 1024-byte swizzle
 // atom) and the tile's elements sit `shift` elements into it.
-template <typename T, bool RG>
+template <typename T, int P, bool RG>
 constexpr int in_bytes() {
-  return Fmt<T>::kBytes + (RG ? 1024 : 0);
+  return Fmt<T, P>::kBytes + (RG ? 1024 : 0);
 }
 
-template <int NIN, int NOUT, int NS, typename T, bool RG = false>
+template <int NIN, int NOUT, int NS, typename T, int P, bool RG>
 struct Smem {
-  alignas(1024) uint8_t in[NS][NIN][in_bytes<T, RG>()];
+  alignas(1024) uint8_t in[NS][NIN][in_bytes<T, P, RG>()];
   // output staging for the TMA stores; ragged tiles store straight from registers
-  alignas(1024) uint8_t out[2][NOUT][RG ? 16 : Fmt<T>::kBytes];
-  StageMeta<NIN, T> meta[NS];
+  alignas(1024) uint8_t out[2][NOUT][RG ? 16 : Fmt<T, P>::kBytes];
+  StageMeta<NIN, T, P> meta[NS];
   uint64_t full[NS];
   uint64_t empty[NS];
   int64_t cu[kCuCache];
@@ -259,9 +261,9 @@ struct Smem {
   int abort;  // a consumer warp gave up: the others stop waiting on it
 };
 
-template <int NIN, int NOUT, int NS, typename T, bool RG = false>
+template <int NIN, int NOUT, int NS, typename T, int P, bool RG>
 constexpr size_t smem_bytes() {
-  return sizeof(Smem<NIN, NOUT, NS, T, RG>) + 1024;  // + alignment slack
+  return sizeof(Smem<NIN, NOUT, NS, T, P, RG>) + 1024;  // + alignment slack
 }
 
 template <typename Sm>
@@ -317,8 +319,8 @@ __device__ __forceinline__ void or_bit(uint32_t* words, uint32_t e) {
 // for the first boundary at or after t, then one pass over the boundaries in
 // [t, t+len]: boundary v = cu[i] starts a sequence at v and ends one at v-1.
 // Called by all lanes.
-template <typename IdxT, int NIN, typename T>
-__device__ __forceinline__ void mark_segment(StageMeta<NIN, T>& m, const CuView<IdxT>& cu,
+template <typename IdxT, int NIN, typename T, int P>
+__device__ __forceinline__ void mark_segment(StageMeta<NIN, T, P>& m, const CuView<IdxT>& cu,
                                              int64_t t, int64_t len, uint32_t pos, int lane,
                                              bool& outside) {
   const int64_t end = t + len;
@@ -352,9 +354,10 @@ __device__ __forceinline__ void mark_segment(StageMeta<NIN, T>& m, const CuView<
 // Builds the boundary bitmaps of the tile that starts at flat index p0, whose
 // first element sits at row position t0 and whose elements end at flat index
 // `limit` (the array end, or the row end in row mode).  Called by all lanes.
-template <typename IdxT, int NIN, typename T>
-__device__ void build_meta(StageMeta<NIN, T>& m, const CuView<IdxT>& cu, int64_t p0, int64_t t0,
+template <typename IdxT, int NIN, typename T, int P>
+__device__ void build_meta(StageMeta<NIN, T, P>& m, const CuView<IdxT>& cu, int64_t p0, int64_t t0,
                            int64_t limit, int64_t n_tma_total, int lane) {
+  constexpr int kTileElems = Geo<P>::kTileElems, kBitWords = Geo<P>::kBitWords;
   const int64_t rem = limit - p0;  // elements of the tile that belong to it (row or array end)
   const uint32_t n_valid = static_cast<uint32_t>(rem < kTileElems ? rem : kTileElems);
   int64_t nt = n_tma_total - p0;
@@ -376,7 +379,7 @@ __device__ void build_meta(StageMeta<NIN, T>& m, const CuView<IdxT>& cu, int64_t
   while (pos < n_valid) {
     int64_t len = static_cast<int64_t>(n_valid - pos);
     if (len > BL - t) len = BL - t;
-    mark_segment<IdxT, NIN, T>(m, cu, t, len, pos, lane, outside);
+    mark_segment<IdxT, NIN, T, P>(m, cu, t, len, pos, lane, outside);
     pos += static_cast<uint32_t>(len);
     t = 0;
   }
@@ -394,8 +397,8 @@ __device__ void build_meta(StageMeta<NIN, T>& m, const CuView<IdxT>& cu, int64_t
 
 // Element e of input k of the current tile, as float (`shift`: elements
 // between the buffer start and the tile start, ragged rows only).
-template <typename T, int NIN>
-__device__ __forceinline__ float tile_elem(const uint8_t* buf, const StageMeta<NIN, T>& m, int k,
+template <typename T, int NIN, int P>
+__device__ __forceinline__ float tile_elem(const uint8_t* buf, const StageMeta<NIN, T, P>& m, int k,
                                            uint32_t e, uint32_t n_tma, uint32_t n_valid,
                                            float fill, uint32_t shift = 0u) {
   if (e < n_tma) return Cvt<T>::to(*reinterpret_cast<const T*>(buf + swz<T>(e + shift)));
@@ -405,10 +408,10 @@ __device__ __forceinline__ float tile_elem(const uint8_t* buf, const StageMeta<N
 
 // Per-thread constants: the swizzled byte offsets of the 16-byte chunks that
 // hold this thread's 16 elements (identical for every 1024-aligned buffer).
-template <typename T>
+template <typename T, int P>
 struct ThreadChunks {
   static constexpr int kVec = 16 / sizeof(T);
-  static constexpr int kChunks = kPerThread / kVec;
+  static constexpr int kChunks = P / kVec;
   uint32_t off[kChunks];
   __device__ __forceinline__ explicit ThreadChunks(uint32_t o) {
 #pragma unroll
@@ -417,18 +420,19 @@ struct ThreadChunks {
 };
 
 // This thread's 16 elements [o, o+16) of input k.
-template <typename T, int NIN>
-__device__ __forceinline__ void read_block(const uint8_t* buf, const ThreadChunks<T>& tc,
-                                           const StageMeta<NIN, T>& m, int k, uint32_t o,
+template <typename T, int NIN, int P>
+__device__ __forceinline__ void read_block(const uint8_t* buf, const ThreadChunks<T, P>& tc,
+                                           const StageMeta<NIN, T, P>& m, int k, uint32_t o,
                                            uint32_t n_tma, uint32_t n_valid, float fill,
-                                           float (&v)[kPerThread]) {
-  if (o + kPerThread <= n_tma) {
+                                           float (&v)[P]) {
+  if (o + P <= n_tma) {
 #pragma unroll
-    for (int c = 0; c < ThreadChunks<T>::kChunks; ++c)
-      unpack16<T>(*reinterpret_cast<const uint4*>(buf + tc.off[c]), &v[c * ThreadChunks<T>::kVec]);
+    for (int c = 0; c < ThreadChunks<T, P>::kChunks; ++c)
+      unpack16<T>(*reinterpret_cast<const uint4*>(buf + tc.off[c]),
+                  &v[c * ThreadChunks<T, P>::kVec]);
   } else {
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j)
+    for (int j = 0; j < P; ++j)
       v[j] = tile_elem<T, NIN>(buf, m, k, o + j, n_tma, n_valid, fill);
   }
 }
@@ -438,24 +442,24 @@ __device__ __forceinline__ void read_block(const uint8_t* buf, const ThreadChunk
 // elements taken from offset r = shift % kVec, which is the same for every
 // thread of the tile (a warp-uniform switch, so no register is indexed at run
 // time).
-template <typename T, int R>
-__device__ __forceinline__ void take_shifted(const float (&raw)[kPerThread + 16 / sizeof(T)],
-                                             float (&v)[kPerThread]) {
+template <typename T, int R, int P>
+__device__ __forceinline__ void take_shifted(const float (&raw)[P + 16 / sizeof(T)],
+                                             float (&v)[P]) {
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j) v[j] = raw[R + j];
+  for (int j = 0; j < P; ++j) v[j] = raw[R + j];
 }
 
-template <typename T, int NIN>
-__device__ __forceinline__ void read_block_shifted(const uint8_t* buf, const StageMeta<NIN, T>& m,
-                                                   int k, uint32_t o, uint32_t shift,
-                                                   uint32_t n_tma, uint32_t n_valid, float fill,
-                                                   float (&v)[kPerThread]) {
-  constexpr int kVec = ThreadChunks<T>::kVec;
-  constexpr int kChunks = ThreadChunks<T>::kChunks;
-  if (o + kPerThread <= n_tma) {
+template <typename T, int NIN, int P>
+__device__ __forceinline__ void read_block_shifted(const uint8_t* buf,
+                                                   const StageMeta<NIN, T, P>& m, int k,
+                                                   uint32_t o, uint32_t shift, uint32_t n_tma,
+                                                   uint32_t n_valid, float fill, float (&v)[P]) {
+  constexpr int kVec = ThreadChunks<T, P>::kVec;
+  constexpr int kChunks = ThreadChunks<T, P>::kChunks;
+  if (o + P <= n_tma) {
     const uint32_t r = shift % kVec;
     const uint32_t base = o + shift - r;
-    float raw[kPerThread + kVec];
+    float raw[P + kVec];
 #pragma unroll
     for (int c = 0; c <= kChunks; ++c)
       unpack16<T>(*reinterpret_cast<const uint4*>(buf + swz<T>(base + c * kVec)), &raw[c * kVec]);
@@ -477,25 +481,25 @@ __device__ __forceinline__ void read_block_shifted(const uint8_t* buf, const Sta
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j)
+    for (int j = 0; j < P; ++j)
       v[j] = tile_elem<T, NIN>(buf, m, k, o + j, n_tma, n_valid, fill, shift);
   }
 }
 
-template <typename T>
-__device__ __forceinline__ void write_block(uint8_t* buf, const ThreadChunks<T>& tc,
-                                            const float (&v)[kPerThread]) {
+template <typename T, int P>
+__device__ __forceinline__ void write_block(uint8_t* buf, const ThreadChunks<T, P>& tc,
+                                            const float (&v)[P]) {
 #pragma unroll
-  for (int c = 0; c < ThreadChunks<T>::kChunks; ++c)
-    *reinterpret_cast<uint4*>(buf + tc.off[c]) = pack16<T>(&v[c * ThreadChunks<T>::kVec]);
+  for (int c = 0; c < ThreadChunks<T, P>::kChunks; ++c)
+    *reinterpret_cast<uint4*>(buf + tc.off[c]) = pack16<T>(&v[c * ThreadChunks<T, P>::kVec]);
 }
 
 // Direct global stores of the elements whose bit is set in `mask`.
-template <typename T>
+template <typename T, int P>
 __device__ __forceinline__ void store_direct(T* base, int64_t p, uint32_t mask,
-                                             const float (&v)[kPerThread]) {
+                                             const float (&v)[P]) {
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j)
+  for (int j = 0; j < P; ++j)
     if ((mask >> j) & 1u) base[p + j] = Cvt<T>::from(v[j]);
 }
 
@@ -506,15 +510,14 @@ __device__ __forceinline__ void store_direct(T* base, int64_t p, uint32_t mask,
 // Lane 0 writes only its own part of its first window (the R elements before
 // q are not the warp's); lane 31's last R elements go out one by one.
 // Warp-collective.
-template <typename T, int R>
-__device__ __forceinline__ void store_window(T* base, int64_t q, const float (&v)[kPerThread],
-                                             int lane) {
-  constexpr int kVec = ThreadChunks<T>::kVec, kChunks = ThreadChunks<T>::kChunks;
-  float w[kPerThread];
+template <typename T, int R, int P>
+__device__ __forceinline__ void store_window(T* base, int64_t q, const float (&v)[P], int lane) {
+  constexpr int kVec = ThreadChunks<T, P>::kVec, kChunks = ThreadChunks<T, P>::kChunks;
+  float w[P];
 #pragma unroll
-  for (int j = 0; j < R; ++j) w[j] = __shfl_up_sync(kFull, v[kPerThread - R + j], 1);
+  for (int j = 0; j < R; ++j) w[j] = __shfl_up_sync(kFull, v[P - R + j], 1);
 #pragma unroll
-  for (int j = R; j < kPerThread; ++j) w[j] = v[j - R];
+  for (int j = R; j < P; ++j) w[j] = v[j - R];
   T* p = base + (q - R);
   if (R == 0 || lane != 0) {
     st_v4(p, pack16<T>(&w[0]));
@@ -526,15 +529,15 @@ __device__ __forceinline__ void store_window(T* base, int64_t q, const float (&v
   for (int c = 1; c < kChunks; ++c) st_v4(p + c * kVec, pack16<T>(&w[c * kVec]));
   if (R != 0 && lane == 31) {
 #pragma unroll
-    for (int j = kPerThread - R; j < kPerThread; ++j) base[q + j] = Cvt<T>::from(v[j]);
+    for (int j = P - R; j < P; ++j) base[q + j] = Cvt<T>::from(v[j]);
   }
 }
 
 // store_window for the run's actual misalignment r = q mod (16 bytes).
-template <typename T>
+template <typename T, int P>
 __device__ __forceinline__ void store_realigned(T* base, int64_t q, uint32_t r,
-                                                const float (&v)[kPerThread], int lane) {
-  constexpr int kVec = ThreadChunks<T>::kVec;
+                                                const float (&v)[P], int lane) {
+  constexpr int kVec = ThreadChunks<T, P>::kVec;
   switch (r) {
     case 0: store_window<T, 0>(base, q, v, lane); break;
     case 1: store_window<T, 1>(base, q, v, lane); break;
@@ -553,9 +556,10 @@ __device__ __forceinline__ void store_realigned(T* base, int64_t q, uint32_t r,
   }
 }
 
-// Bits j of [0, kPerThread) with o + j < limit.
+// Bits j of [0, P) with o + j < limit.
+template <int P>
 __device__ __forceinline__ uint32_t below_mask(uint32_t o, uint32_t limit) {
-  if (limit >= o + kPerThread) return kThreadMask;
+  if (limit >= o + P) return Geo<P>::kMask;
   return limit > o ? (1u << (limit - o)) - 1u : 0u;
 }
 
@@ -563,9 +567,9 @@ __device__ __forceinline__ uint32_t below_mask(uint32_t o, uint32_t limit) {
 // local inclusive prefix of every element in place (a[j] = product of the
 // gates since the last head, b[j] = the state from a zero carry) and returns
 // the thread's aggregate.  Two independent chains (a and b).
-template <bool REV>
-__device__ __forceinline__ Pfx fold16_inplace(float (&a)[kPerThread], float (&b)[kPerThread],
-                                              uint32_t head) {
+template <bool REV, int P>
+__device__ __forceinline__ Pfx fold16_inplace(float (&a)[P], float (&b)[P], uint32_t head) {
+  constexpr int kPerThread = P;
   constexpr int j0 = REV ? kPerThread - 1 : 0;
   float A = a[j0], B = b[j0];
   const int f = kValid | (head != 0u ? kHead : 0);
@@ -598,11 +602,11 @@ __device__ __forceinline__ Pfx fold16_inplace(float (&a)[kPerThread], float (&b)
 
 // Elements (bits) that come before the first head in scan order: only these
 // take the carry-in.
-template <bool REV>
+template <bool REV, int P>
 __device__ __forceinline__ uint32_t carry_mask(uint32_t head) {
-  if (head == 0u) return kThreadMask;
+  if (head == 0u) return Geo<P>::kMask;
   if (!REV) return (1u << (__ffs(head) - 1)) - 1u;
-  return kThreadMask & ~((2u << (31 - __clz(head))) - 1u);
+  return Geo<P>::kMask & ~((2u << (31 - __clz(head))) - 1u);
 }
 
 // ---- time slabs: per-row carry-in, halo and aggregate --------------------
@@ -617,12 +621,11 @@ __device__ __forceinline__ int64_t row_at(int64_t q, int64_t BL, int64_t want) {
 // first element in scan order, which is a sequence head: x' = x + g * state
 // and g' = g * product reproduce the continued recurrence and its gate
 // products exactly.  `bits` holds the thread's heads.
-template <bool REV>
-__device__ __forceinline__ void apply_row_carry(float (&a)[kPerThread], float (&b)[kPerThread],
-                                                uint32_t bits, int64_t p, int64_t BL,
-                                                const float* carry) {
+template <bool REV, int K>
+__device__ __forceinline__ void apply_row_carry(float (&a)[K], float (&b)[K], uint32_t bits,
+                                                int64_t p, int64_t BL, const float* carry) {
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j) {
+  for (int j = 0; j < K; ++j) {
     if ((bits >> j) & 1u) {
       const int64_t r = row_at(p + j, BL, REV ? BL - 1 : 0);
       if (r >= 0) {
@@ -637,12 +640,12 @@ __device__ __forceinline__ void apply_row_carry(float (&a)[kPerThread], float (&
 // scan order (a head: the end of the slab's last sequence piece); its
 // successor gate lives outside the slab and is already part of the term, so
 // the element's own coefficient becomes the identity.
-template <bool CAUSAL>
-__device__ __forceinline__ void apply_row_carry_adjoint(float (&a)[kPerThread],
-                                                        float (&b)[kPerThread], uint32_t bits,
-                                                        int64_t p, int64_t BL, const float* carry) {
+template <bool CAUSAL, int K>
+__device__ __forceinline__ void apply_row_carry_adjoint(float (&a)[K], float (&b)[K],
+                                                        uint32_t bits, int64_t p, int64_t BL,
+                                                        const float* carry) {
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j) {
+  for (int j = 0; j < K; ++j) {
     if ((bits >> j) & 1u) {
       const int64_t r = row_at(p + j, BL, CAUSAL ? BL - 1 : 0);
       if (r >= 0) {
@@ -656,12 +659,12 @@ __device__ __forceinline__ void apply_row_carry_adjoint(float (&a)[kPerThread],
 // Backward: the state neighbour of the row element whose neighbour lies
 // outside the slab.  Returns the bits that took a halo (their gate gradient
 // is not forced to zero).
-template <bool CAUSAL>
-__device__ __forceinline__ uint32_t apply_row_halo(float (&hv)[kPerThread], uint32_t bits,
-                                                   int64_t p, int64_t BL, const float* halo) {
+template <bool CAUSAL, int K>
+__device__ __forceinline__ uint32_t apply_row_halo(float (&hv)[K], uint32_t bits, int64_t p,
+                                                   int64_t BL, const float* halo) {
   uint32_t used = 0u;
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j) {
+  for (int j = 0; j < K; ++j) {
     if ((bits >> j) & 1u) {
       const int64_t r = row_at(p + j, BL, CAUSAL ? 0 : BL - 1);
       if (r >= 0) {
@@ -676,13 +679,12 @@ __device__ __forceinline__ uint32_t apply_row_halo(float (&hv)[kPerThread], uint
 // Inclusive (gate product, value) at each row's last element in scan order.
 // a, b are the thread's local prefixes and P its exclusive prefix; elements in
 // `cm` (before the thread's first head) take P.
-template <bool REV>
-__device__ __forceinline__ void record_row_agg(const float (&a)[kPerThread],
-                                               const float (&b)[kPerThread], uint32_t bits,
-                                               uint32_t cm, const Pfx& P, int64_t p, int64_t BL,
-                                               float* agg) {
+template <bool REV, int K>
+__device__ __forceinline__ void record_row_agg(const float (&a)[K], const float (&b)[K],
+                                               uint32_t bits, uint32_t cm, const Pfx& P,
+                                               int64_t p, int64_t BL, float* agg) {
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j) {
+  for (int j = 0; j < K; ++j) {
     if ((bits >> j) & 1u) {
       const int64_t r = row_at(p + j, BL, REV ? 0 : BL - 1);
       if (r >= 0) {
