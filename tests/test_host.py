@@ -92,6 +92,15 @@ def test_bidi_abi_refuses_crossed_buffers_without_a_gpu():
   assert lib.ascan_workspace_size_bidi(7, 4097, 0) == 2 * 512  # two 256-aligned halves
 
 
+def test_tile_width_knob_without_a_gpu():
+  assert _lib.get_tile_width() == 0
+  with pytest.raises(ValueError):
+    _lib.set_tile_width(24)
+  _lib.set_tile_width(32)
+  assert _lib.get_tile_width() == 32
+  _lib.set_tile_width(0)
+
+
 def test_ops_refuse_cpu_tensors():
   g = torch.rand(2, 8)
   x = torch.rand(2, 8)

@@ -92,10 +92,11 @@ def _bidi_inputs(C, BL, dtype, seed):
   return [t.to(DEV, dtype) for t in ts]  # gf, xf, gb, xb, dyf, dyb
 
 
+@pytest.mark.parametrize("width", [0, 16, 32])
 @pytest.mark.parametrize("impl", ["auto", "tma-flat", "simple"])
 @pytest.mark.parametrize(("C", "seqlens"), BIDI_FUSED_CASES)
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
-def test_fused_bidi_launch_matches_two_launches(impl, C, seqlens, dtype):
+def test_fused_bidi_launch_matches_two_launches(width, impl, C, seqlens, dtype):
   """One launch for both directions (ascan_forward_bidi / ascan_backward_bidi)
   against the two single-direction launches it replaces; bit for bit where no
   tile needs a look-back (the same arithmetic), else to float rounding."""
@@ -106,6 +107,7 @@ def test_fused_bidi_launch_matches_two_launches(impl, C, seqlens, dtype):
   e = torch.empty_like
   try:
     _lib.set_implementation(impl)
+    _lib.set_tile_width(width)
     yf, yb = e(xf), e(xb)
     _lib.forward_bidi(gf, xf, yf, gb, xb, yb, cu, S, C)
     d = [e(xf) for _ in range(4)]
@@ -118,6 +120,7 @@ def test_fused_bidi_launch_matches_two_launches(impl, C, seqlens, dtype):
     _lib.backward(dyb, gb, yb2, d2[2], d2[3], cu, S, C, False)
     torch.cuda.synchronize()
   finally:
+    _lib.set_tile_width(0)
     _lib.set_implementation("auto")
   _lib.check_device_error()
   got, want = [yf, yb, *d], [yf2, yb2, *d2]

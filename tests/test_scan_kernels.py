@@ -587,3 +587,51 @@ def test_flat_sized_workspace_is_accepted(reverse):
   gold_y, _ = oracle.scan_fwd(g, x, cu, reverse=reverse)
   assert_close_to_gold(y, gold_y, torch.float32, "flat-sized workspace")
   assert call(flat_bytes - 1) == -2  # ASCAN_EWORKSPACE: one byte short of the flat size
+
+
+WIDE_TILE_CASES = [
+  # C, cu_seqlens: flat order, row order (aligned and ragged), look-back
+  (64, [0, 8192 * 2]),
+  (300, [0, 4096, 8192 * 2 + 5, 8192 * 3]),
+  (5, [0, 8192 * 3 + 77]),
+  (33, [0, 1, 5000, 9001, 30000]),
+  (3, [0, 100]),
+  (2, [100, 300, 16389]),
+]
+
+
+@pytest.mark.parametrize("order", ["tma", "tma-row", "tma-flat"])
+@pytest.mark.parametrize(("C", "cu_list"), WIDE_TILE_CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_wide_tiles_match_oracle(order, C, cu_list, dtype, reverse):
+  """8192-element tiles (32 elements per consumer thread), forced: the forward
+  of every dtype and the 16-bit backward run them (the fp32 backward and the
+  gate-product forward stay at 4096), against the oracle."""
+  from associative_scan_triton import _lib
+  BL = cu_list[-1]
+  S = len(cu_list) - 1
+  g, x = make_inputs(C, BL, dtype=dtype, gate="long", seed=C + BL + 7)
+  cu = torch.tensor(cu_list, dtype=torch.int64, device=DEV)
+  mask = in_sequence_mask(C, BL, cu)
+  dy = torch.randn(C, BL, generator=torch.Generator().manual_seed(8)).to(DEV, dtype)
+  try:
+    _lib.set_implementation(order)
+    _lib.set_tile_width(32)
+    y = torch.full_like(x, 7.0)
+    ast.forward_scan_full(g, x, cu, (S, 1, C), REVERSE=reverse, CHUNK_SIZE=2, TESTING=False,
+                          tokens_out=y)
+    dx, dg = torch.full_like(x, 7.0), torch.full_like(x, 7.0)
+    ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, (S, 1, C), CHUNK_SIZE=2,
+                                 CAUSAL=not reverse)
+    torch.cuda.synchronize()
+  finally:
+    _lib.set_tile_width(0)
+    _lib.set_implementation("auto")
+  _lib.check_device_error()
+  gold_y, _ = oracle.scan_fwd(g, x, cu, reverse=reverse)
+  assert_close_to_gold(y, gold_y, dtype, "wide tiles y", mask=mask)
+  gdx, gdg = oracle.scan_bwd(dy, g, y, cu, causal=not reverse)
+  assert_close_to_gold(dx, gdx, dtype, "wide tiles dx", mask=mask)
+  assert_close_to_gold(dg, gdg, dtype, "wide tiles dg", mask=mask)
+  assert (y[:, ~mask[0]] == 7.0).all() and (dx[:, ~mask[0]] == 7.0).all()
