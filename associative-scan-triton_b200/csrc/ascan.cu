@@ -1416,19 +1416,25 @@ static int g_tile_width = 0;
 
 // Whether a launch runs 8192-element tiles (32 elements per thread) rather
 // than 4096-element ones.  Wide tiles halve the consumer warps' fixed
-// per-tile chain (fold, warp scan, hand-offs, carry) per byte: measured on
-// B200 the fp32 forward at B=8, C=1536 goes from 143 to 106 us (T=4096) and
-// from 2264 to 1483 us (T=65536), and the fp16 forward and backward at
-// T=2048 from 76/92 to 55/69 us.  They lose when rows are few (each row's
-// tiles form a serial chain: C=257, T=100003 went from 119 to 204 us), when
-// there are too few tiles to fill the SMs, and in ragged forward rows.
-static bool use_wide(int64_t N, int64_t BL, int64_t S, bool allow_ragged, bool ragged_ok) {
+// per-tile chain (fold, warp scan, hand-offs, carry) per byte.  Measured on
+// B200 (fwd / bwd, us): B=8, C=1536, fp32 T=4096 fwd 143 -> 106, T=65536
+// 2267 -> 1481; bf16 T=4096 139/173 -> 99/130; fp16 T=2048 76/92 -> 55/69;
+// C=256, T=2^20 fwd 868 -> 559.  They lose in ragged forward rows (C=257,
+// T=100003: 119 -> 201), when they would turn a row order into a flat one
+// for the forward (varlen C=2048: 1150 -> 1196), and gain nothing when the
+// tiles are too few to fill the SMs twice.  Rows fewer than the CTAs would
+// put a tile's predecessor in its own wave.
+static bool use_wide(int64_t N, int64_t BL, int64_t S, bool allow_ragged, bool forward) {
   if (g_tile_width != 0) return g_tile_width == 32;
-  const tma::TileSched sch = make_sched(tma::Geo<32>::kTileElems, N, BL, S, allow_ragged);
-  if (sch.ragged && !ragged_ok) return false;
+  const tma::TileSched wide = make_sched(tma::Geo<32>::kTileElems, N, BL, S, allow_ragged);
+  if (forward) {
+    if (wide.ragged) return false;
+    const tma::TileSched narrow = make_sched(tma::Geo<16>::kTileElems, N, BL, S, allow_ragged);
+    if (narrow.row_mode && !wide.row_mode) return false;
+  }
   const uint32_t sms = static_cast<uint32_t>(sm_count());
-  if (sms == 0 || sch.num_tiles < 2 * sms) return false;
-  if (sch.row_mode && sch.rows < 4 * sms) return false;
+  if (sms == 0 || wide.num_tiles < 2 * sms) return false;
+  if (wide.row_mode && wide.rows < sms) return false;
   return true;
 }
 
@@ -1490,7 +1496,7 @@ static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, bool allow_ragged, cudaStre
   const bool io = a.io.carry || a.io.halo || a.io.agg || !a.y;
   // wide tiles for the plain forward (the gate-product output stays narrow)
   if constexpr (!GOUT) {
-    if (!io && use_wide(a.N, a.BL, a.S, allow_ragged, false))
+    if (!io && use_wide(a.N, a.BL, a.S, allow_ragged, /*forward=*/true))
       return launch_fwd_tma_p<T, IdxT, REV, GOUT, 32>(a, allow_ragged, io, s);
   }
   return launch_fwd_tma_p<T, IdxT, REV, GOUT, 16>(a, allow_ragged, io, s);
@@ -1550,7 +1556,7 @@ template <typename T, typename IdxT, bool CAUSAL>
 static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, bool allow_ragged, cudaStream_t s) {
   const bool io = a.io.carry || a.io.halo || a.io.agg || !a.dx;
   if constexpr (kWideBwd<T>) {
-    if (!io && use_wide(a.N, a.BL, a.S, allow_ragged, true))
+    if (!io && use_wide(a.N, a.BL, a.S, allow_ragged, /*forward=*/false))
       return launch_bwd_tma_p<T, IdxT, CAUSAL, 32>(a, allow_ragged, io, s);
   }
   return launch_bwd_tma_p<T, IdxT, CAUSAL, 16>(a, allow_ragged, io, s);
@@ -1781,7 +1787,7 @@ static int fwd_bidi_typed(const void* gf, const void* xf, void* yf, const void* 
       a.io = RowIO{nullptr, nullptr, nullptr};
     }
     const bool ragged_ok = wf.allow_ragged && wb.allow_ragged;
-    const int rc = use_wide(N, BL, S, ragged_ok, false)
+    const int rc = use_wide(N, BL, S, ragged_ok, /*forward=*/true)
                        ? launch_fwd_bidi_p<T, IdxT, 32>(fa, ba, ragged_ok, s)
                        : launch_fwd_bidi_p<T, IdxT, 16>(fa, ba, ragged_ok, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
@@ -1824,7 +1830,7 @@ static int bwd_bidi_typed(const void* const (&in)[2][3], void* const (&out)[2][2
     const bool ragged_ok = wf.allow_ragged && wb.allow_ragged;
     int rc;
     if constexpr (kWideBwd<T>)
-      rc = use_wide(N, BL, S, ragged_ok, true)
+      rc = use_wide(N, BL, S, ragged_ok, /*forward=*/false)
                ? launch_bwd_bidi_p<T, IdxT, 32>(fa, ba, ragged_ok, s)
                : launch_bwd_bidi_p<T, IdxT, 16>(fa, ba, ragged_ok, s);
     else
