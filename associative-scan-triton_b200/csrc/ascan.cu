@@ -1429,8 +1429,10 @@ static bool use_wide(int64_t N, int64_t BL, int64_t S, bool allow_ragged, bool f
   const tma::TileSched wide = make_sched(tma::Geo<32>::kTileElems, N, BL, S, allow_ragged);
   if (forward) {
     if (wide.ragged) return false;
+    // keep the narrow row order unless sequences average a whole wide tile
+    // (then the wide flat tiles mostly start at sequence heads)
     const tma::TileSched narrow = make_sched(tma::Geo<16>::kTileElems, N, BL, S, allow_ragged);
-    if (narrow.row_mode && !wide.row_mode) return false;
+    if (narrow.row_mode && !wide.row_mode && BL < S * tma::Geo<32>::kTileElems) return false;
   }
   const uint32_t sms = static_cast<uint32_t>(sm_count());
   if (sms == 0 || wide.num_tiles < 2 * sms) return false;
