@@ -1463,7 +1463,7 @@ static int launch_fwd_tma_sched(const FwdArgs<T, IdxT>& a, const tma::TileSched&
     mgo = my;
   }
   const void* kern;
-  if constexpr (RG || P != 16)  // slab I/O: staged 4096-element kernels only
+  if constexpr (RG)  // slab I/O exists in the staged kernels only
     kern = reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, false, P, RG>);
   else
     kern = io ? reinterpret_cast<const void*>(scan_fwd_tma_kernel<T, IdxT, REV, GOUT, NS, true, P, false>)
@@ -1498,7 +1498,7 @@ static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, bool allow_ragged, cudaStre
   const bool io = a.io.carry || a.io.halo || a.io.agg || !a.y;
   // wide tiles for the plain forward (the gate-product output stays narrow)
   if constexpr (!GOUT) {
-    if (!io && use_wide(a.N, a.BL, a.S, allow_ragged, /*forward=*/true))
+    if (use_wide(a.N, a.BL, a.S, allow_ragged && !io, /*forward=*/true))
       return launch_fwd_tma_p<T, IdxT, REV, GOUT, 32>(a, allow_ragged, io, s);
   }
   return launch_fwd_tma_p<T, IdxT, REV, GOUT, 16>(a, allow_ragged, io, s);
@@ -1521,7 +1521,7 @@ static int launch_bwd_tma_sched(const BwdArgs<T, IdxT>& a, const tma::TileSched&
       !make_map<T>(&mdg, a.dg ? a.dg : a.dy, rows, kPart))
     return 0;
   const void* kern;
-  if constexpr (RG || P != 16)
+  if constexpr (RG)
     kern = reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, false, P, RG>);
   else
     kern = io ? reinterpret_cast<const void*>(scan_bwd_tma_kernel<T, IdxT, CAUSAL, NS, true, P, false>)
@@ -1558,7 +1558,7 @@ template <typename T, typename IdxT, bool CAUSAL>
 static int launch_bwd_tma(const BwdArgs<T, IdxT>& a, bool allow_ragged, cudaStream_t s) {
   const bool io = a.io.carry || a.io.halo || a.io.agg || !a.dx;
   if constexpr (kWideBwd<T>) {
-    if (!io && use_wide(a.N, a.BL, a.S, allow_ragged, /*forward=*/false))
+    if (use_wide(a.N, a.BL, a.S, allow_ragged && !io, /*forward=*/false))
       return launch_bwd_tma_p<T, IdxT, CAUSAL, 32>(a, allow_ragged, io, s);
   }
   return launch_bwd_tma_p<T, IdxT, CAUSAL, 16>(a, allow_ragged, io, s);

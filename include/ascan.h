@@ -278,9 +278,10 @@ ASCAN_API int ascan_get_implementation(void);
  * Tile width of the persistent kernels, for tests and tuning (no
  * counterpart in the reference): 0 (default) chooses per launch, 16 or 32
  * forces 4096- or 8192-element tiles (16 or 32 elements per consumer
- * thread) wherever the library has both kernels -- the plain forward of
- * every dtype and the backward of fp16/bf16; other launches, and time-slab
- * launches, always use 16.  Process-wide; results agree up to rounding.
+ * thread) wherever the library has both kernels -- the forward of every
+ * dtype without gates_out, and the backward of fp16/bf16 (time slabs
+ * included); other launches always use 16.  Process-wide; results agree up
+ * to rounding.
  */
 ASCAN_API int ascan_set_tile_width(int elems_per_thread);
 ASCAN_API int ascan_get_tile_width(void);

@@ -168,9 +168,19 @@ CASES = [
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("width", [0, 32])
 @pytest.mark.parametrize(("C", "T", "world", "cu"), CASES)
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_emulated_slabs_match_oracle(C, T, world, cu, dtype):
+def test_emulated_slabs_match_oracle(C, T, world, cu, dtype, width):
+  from associative_scan_triton import _lib
+  _lib.set_tile_width(width)  # 32: the slab kernels on 8192-element tiles
+  try:
+    _emulated_slabs_match_oracle(C, T, world, cu, dtype)
+  finally:
+    _lib.set_tile_width(0)
+
+
+def _emulated_slabs_match_oracle(C, T, world, cu, dtype):
   g, x = make_inputs(C, T, dtype=dtype, gate="verylong", seed=C + T + world)
   dy = torch.randn(C, T, generator=torch.Generator().manual_seed(3)).to("cuda", dtype)
   bounds = ts.even_bounds(T, world, align=64)
