@@ -1386,8 +1386,10 @@ static bool split_bidi(int cap, tma::TileSched& fs, tma::TileSched& bs, uint32_t
 // allow_ragged: rows that are not whole tiles may be cut into whole tiles and
 // a partial last one (the workspace has their status slots and the launch
 // has no slab I/O).
+// row_hint: take the row order whenever it fits, as if sequences were long
+// (wide tiles keep the order the narrow ones would have chosen).
 static tma::TileSched make_sched(int64_t kT, int64_t N, int64_t BL, int64_t S,
-                                 bool allow_ragged) {
+                                 bool allow_ragged, bool row_hint = false) {
   tma::TileSched sch{static_cast<uint32_t>((N + kT - 1) / kT), 0u, 0u, 0u, 1u, 0u, 0u, 0u};
   const int64_t C = BL > 0 ? N / BL : 0;
   const int mode = impl_mode();
@@ -1396,7 +1398,7 @@ static tma::TileSched make_sched(int64_t kT, int64_t N, int64_t BL, int64_t S,
   const bool fits = BL >= kT && C >= 1 && C <= 0x7fffffffll && C * per_row <= 0xffffffffll &&
                     (aligned || allow_ragged);
   const bool long_seqs = BL > S * kT;  // mean length above a tile
-  const bool row = mode == 4 ? fits : mode == 3 ? false : fits && long_seqs;
+  const bool row = mode == 4 ? fits : mode == 3 ? false : fits && (long_seqs || row_hint);
   if (row) {
     sch.row_mode = 1u;
     sch.rows = static_cast<uint32_t>(C);
@@ -1424,15 +1426,25 @@ static int g_tile_width = 0;
 // for the forward (varlen C=2048: 1150 -> 1196), and gain nothing when the
 // tiles are too few to fill the SMs twice.  Rows fewer than the CTAs would
 // put a tile's predecessor in its own wave.
-static bool use_wide(int64_t N, int64_t BL, int64_t S, bool allow_ragged, bool forward) {
+static bool use_wide(int64_t N, int64_t BL, int64_t S, bool allow_ragged, bool forward,
+                     bool narrow_type = false, bool* row_hint = nullptr) {
+  if (row_hint) *row_hint = false;
   if (g_tile_width != 0) return g_tile_width == 32;
-  const tma::TileSched wide = make_sched(tma::Geo<32>::kTileElems, N, BL, S, allow_ragged);
+  tma::TileSched wide = make_sched(tma::Geo<32>::kTileElems, N, BL, S, allow_ragged);
   if (forward) {
-    if (wide.ragged) return false;
     // keep the narrow row order unless sequences average a whole wide tile
-    // (then the wide flat tiles mostly start at sequence heads)
+    // (then the wide flat tiles mostly start at sequence heads); 16-bit
+    // types keep it with wide tiles (ragged rows included)
     const tma::TileSched narrow = make_sched(tma::Geo<16>::kTileElems, N, BL, S, allow_ragged);
-    if (narrow.row_mode && !wide.row_mode && BL < S * tma::Geo<32>::kTileElems) return false;
+    if (narrow.row_mode && !wide.row_mode && BL < S * tma::Geo<32>::kTileElems) {
+      if (!narrow_type || !row_hint) return false;
+      wide = make_sched(tma::Geo<32>::kTileElems, N, BL, S, allow_ragged, true);
+      if (!wide.row_mode) return false;
+      *row_hint = true;
+    }
+    // fp32 ragged rows at the wide width store 128 bytes per lane from
+    // registers, which measured slower than the narrow tiles
+    if (wide.ragged && !narrow_type) return false;
   }
   const uint32_t sms = static_cast<uint32_t>(sm_count());
   if (sms == 0 || wide.num_tiles < 2 * sms) return false;
@@ -1478,10 +1490,10 @@ static int launch_fwd_tma_sched(const FwdArgs<T, IdxT>& a, const tma::TileSched&
 
 template <typename T, typename IdxT, bool REV, bool GOUT, int P>
 static int launch_fwd_tma_p(const FwdArgs<T, IdxT>& a, bool allow_ragged, bool io,
-                            cudaStream_t s) {
+                            cudaStream_t s, bool row_hint = false) {
   // ragged rows need the shifted-tile kernels, which exist without slab I/O only
   const tma::TileSched sch =
-      make_sched(tma::Geo<P>::kTileElems, a.N, a.BL, a.S, allow_ragged && !io);
+      make_sched(tma::Geo<P>::kTileElems, a.N, a.BL, a.S, allow_ragged && !io, row_hint);
   constexpr bool kStaged = staged_fits<T, 2, GOUT ? 2 : 1, P>();
   if (sch.ragged || !kStaged) {
     if (io) return 0;  // slab I/O exists in the staged kernels only
@@ -1498,8 +1510,10 @@ static int launch_fwd_tma(const FwdArgs<T, IdxT>& a, bool allow_ragged, cudaStre
   const bool io = a.io.carry || a.io.halo || a.io.agg || !a.y;
   // wide tiles for the plain forward (the gate-product output stays narrow)
   if constexpr (!GOUT) {
-    if (use_wide(a.N, a.BL, a.S, allow_ragged && !io, /*forward=*/true))
-      return launch_fwd_tma_p<T, IdxT, REV, GOUT, 32>(a, allow_ragged, io, s);
+    bool row_hint = false;
+    if (use_wide(a.N, a.BL, a.S, allow_ragged && !io, /*forward=*/true, sizeof(T) == 2,
+                 &row_hint))
+      return launch_fwd_tma_p<T, IdxT, REV, GOUT, 32>(a, allow_ragged, io, s, row_hint);
   }
   return launch_fwd_tma_p<T, IdxT, REV, GOUT, 16>(a, allow_ragged, io, s);
 }
@@ -1741,8 +1755,9 @@ static int launch_bwd_bidi_sched(const BwdArgs<T, IdxT>& fa, const BwdArgs<T, Id
 // Tile order and kernel variant of a bidirectional launch at tile width P.
 template <typename T, typename IdxT, int P>
 static int launch_fwd_bidi_p(const FwdArgs<T, IdxT>& fa, const FwdArgs<T, IdxT>& ba,
-                             bool allow_ragged, cudaStream_t s) {
-  const tma::TileSched sch = make_sched(tma::Geo<P>::kTileElems, fa.N, fa.BL, fa.S, allow_ragged);
+                             bool allow_ragged, cudaStream_t s, bool row_hint = false) {
+  const tma::TileSched sch =
+      make_sched(tma::Geo<P>::kTileElems, fa.N, fa.BL, fa.S, allow_ragged, row_hint);
   if constexpr (staged_fits<T, 2, 1, P>()) {
     if (!sch.ragged) return launch_fwd_bidi_sched<T, IdxT, P, false>(fa, ba, sch, sch, s);
   }
@@ -1789,8 +1804,9 @@ static int fwd_bidi_typed(const void* gf, const void* xf, void* yf, const void* 
       a.io = RowIO{nullptr, nullptr, nullptr};
     }
     const bool ragged_ok = wf.allow_ragged && wb.allow_ragged;
-    const int rc = use_wide(N, BL, S, ragged_ok, /*forward=*/true)
-                       ? launch_fwd_bidi_p<T, IdxT, 32>(fa, ba, ragged_ok, s)
+    bool row_hint = false;
+    const int rc = use_wide(N, BL, S, ragged_ok, /*forward=*/true, sizeof(T) == 2, &row_hint)
+                       ? launch_fwd_bidi_p<T, IdxT, 32>(fa, ba, ragged_ok, s, row_hint)
                        : launch_fwd_bidi_p<T, IdxT, 16>(fa, ba, ragged_ok, s);
     if (rc != 0) return rc > 0 ? ASCAN_OK : rc;
   }
