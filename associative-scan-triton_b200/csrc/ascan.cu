@@ -712,8 +712,9 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
       if (__all_sync(kFull, direct == kThreadMask)) {
         // ragged rows: a wholly valid warp slice leaves by realigned 16-byte stores
         const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T, P>::kVec);
-        store_realigned<T>(args.y, p0 + o, r, b, lane);
-        if constexpr (GATES_OUT) store_realigned<T>(args.gout, p0 + o, r, a, lane);
+        store_realigned<T>(args.y, p0 + o, r, b, lane, warp_stage(sm, 0, warp));
+        if constexpr (GATES_OUT)
+          store_realigned<T>(args.gout, p0 + o, r, a, lane, warp_stage(sm, 1, warp));
         direct = 0u;
       }
     }
@@ -971,8 +972,8 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
       if (__all_sync(kFull, direct == kThreadMask)) {
         // ragged rows: a wholly valid warp slice leaves by realigned 16-byte stores
         const uint32_t r = static_cast<uint32_t>(p0 % ThreadChunks<T, P>::kVec);
-        store_realigned<T>(args.dx, p0 + o, r, dyv, lane);
-        store_realigned<T>(args.dg, p0 + o, r, gv, lane);
+        store_realigned<T>(args.dx, p0 + o, r, dyv, lane, warp_stage(sm, 0, warp));
+        store_realigned<T>(args.dg, p0 + o, r, gv, lane, warp_stage(sm, 1, warp));
         direct = 0u;
       }
     }

@@ -251,8 +251,10 @@ constexpr int in_bytes() {
 template <int NIN, int NOUT, int NS, typename T, int P, bool RG>
 struct Smem {
   alignas(1024) uint8_t in[NS][NIN][in_bytes<T, P, RG>()];
-  // output staging for the TMA stores; ragged tiles store straight from registers
-  alignas(1024) uint8_t out[2][NOUT][RG ? 16 : Fmt<T, P>::kBytes];
+  // output staging: double-buffered tiles for the TMA stores, or (RG) one
+  // tile per output cut into per-warp buffers for the coalesced register
+  // stores of store_window
+  alignas(1024) uint8_t out[2][NOUT][RG ? Fmt<T, P>::kBytes / 2 : Fmt<T, P>::kBytes];
   StageMeta<NIN, T, P> meta[NS];
   uint64_t full[NS];
   uint64_t empty[NS];
@@ -260,6 +262,13 @@ struct Smem {
   XSlot xs[kXsRing];
   int abort;  // a consumer warp gave up: the others stop waiting on it
 };
+
+// RG kernels: warp w's staging buffer for output k (32 P elements).
+template <int NIN, int NOUT, int NS, typename T, int P, bool RG>
+__device__ __forceinline__ uint8_t* warp_stage(Smem<NIN, NOUT, NS, T, P, RG>& sm, int k, int warp) {
+  constexpr int kWarpBytes = Fmt<T, P>::kBytes / kConsumerWarps;
+  return &sm.out[0][0][0] + k * Fmt<T, P>::kBytes + warp * kWarpBytes;
+}
 
 template <int NIN, int NOUT, int NS, typename T, int P, bool RG>
 constexpr size_t smem_bytes() {
@@ -503,53 +512,68 @@ __device__ __forceinline__ void store_direct(T* base, int64_t p, uint32_t mask,
     if ((mask >> j) & 1u) base[p + j] = Cvt<T>::from(v[j]);
 }
 
-// Lane t holds the 16 elements [q + 16 t, q + 16 t + 16) of a warp-contiguous
-// run whose start q lies R elements past a 16-byte boundary.  Every lane takes
-// the last R elements of its left neighbour, so that it holds the aligned
-// window [q + 16 t - R, q + 16 t - R + 16), and writes it with 16-byte stores.
-// Lane 0 writes only its own part of its first window (the R elements before
-// q are not the warp's); lane 31's last R elements go out one by one.
+// Lane t holds the P elements [q + P t, q + P t + P) of a warp-contiguous
+// run whose start q (lane 0's) lies R elements past a 16-byte boundary.
+// Every lane takes the last R elements of its left neighbour, so that it
+// holds the aligned window [q + P t - R, q + P t - R + P); the windows go
+// through the warp's staging buffer `stage` (32 P elements, 128B-swizzled)
+// and leave as 16-byte stores in which consecutive lanes write consecutive
+// chunks (a fully coalesced 512-byte run per instruction).  The R elements
+// before q are not the warp's: the first chunk is written element by
+// element from R on; lane 31's last R elements go out one by one.
 // Warp-collective.
 template <typename T, int R, int P>
-__device__ __forceinline__ void store_window(T* base, int64_t q, const float (&v)[P], int lane) {
+__device__ __forceinline__ void store_window(T* base, int64_t q_lane, const float (&v)[P],
+                                             int lane, uint8_t* stage) {
   constexpr int kVec = ThreadChunks<T, P>::kVec, kChunks = ThreadChunks<T, P>::kChunks;
   float w[P];
 #pragma unroll
   for (int j = 0; j < R; ++j) w[j] = __shfl_up_sync(kFull, v[P - R + j], 1);
 #pragma unroll
   for (int j = R; j < P; ++j) w[j] = v[j - R];
-  T* p = base + (q - R);
-  if (R == 0 || lane != 0) {
-    st_v4(p, pack16<T>(&w[0]));
-  } else {
+  const uint32_t e0 = static_cast<uint32_t>(lane) * P;
 #pragma unroll
-    for (int j = R; j < kVec; ++j) p[j] = Cvt<T>::from(w[j]);
+  for (int c = 0; c < kChunks; ++c)
+    *reinterpret_cast<uint4*>(stage + swz<T>(e0 + c * kVec)) = pack16<T>(&w[c * kVec]);
+  __syncwarp();
+  const int64_t w0 = q_lane - static_cast<int64_t>(e0) - R;  // the warp's aligned window start
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    const uint32_t ci = static_cast<uint32_t>(lane) + 32u * k;  // chunk of the warp's window
+    const uint4 val = *reinterpret_cast<const uint4*>(stage + swz<T>(ci * kVec));
+    T* dst = base + w0 + static_cast<int64_t>(ci) * kVec;
+    if (R != 0 && ci == 0u) {
+      const T* e = reinterpret_cast<const T*>(&val);
+#pragma unroll
+      for (int j = R; j < kVec; ++j) dst[j] = e[j];
+    } else {
+      st_v4(dst, val);
+    }
   }
-#pragma unroll
-  for (int c = 1; c < kChunks; ++c) st_v4(p + c * kVec, pack16<T>(&w[c * kVec]));
   if (R != 0 && lane == 31) {
 #pragma unroll
-    for (int j = P - R; j < P; ++j) base[q + j] = Cvt<T>::from(v[j]);
+    for (int j = P - R; j < P; ++j) base[q_lane + j] = Cvt<T>::from(v[j]);
   }
+  __syncwarp();  // the buffer is free again for the next output
 }
 
 // store_window for the run's actual misalignment r = q mod (16 bytes).
 template <typename T, int P>
 __device__ __forceinline__ void store_realigned(T* base, int64_t q, uint32_t r,
-                                                const float (&v)[P], int lane) {
+                                                const float (&v)[P], int lane, uint8_t* stage) {
   constexpr int kVec = ThreadChunks<T, P>::kVec;
   switch (r) {
-    case 0: store_window<T, 0>(base, q, v, lane); break;
-    case 1: store_window<T, 1>(base, q, v, lane); break;
-    case 2: store_window<T, 2>(base, q, v, lane); break;
-    case 3: store_window<T, 3>(base, q, v, lane); break;
+    case 0: store_window<T, 0>(base, q, v, lane, stage); break;
+    case 1: store_window<T, 1>(base, q, v, lane, stage); break;
+    case 2: store_window<T, 2>(base, q, v, lane, stage); break;
+    case 3: store_window<T, 3>(base, q, v, lane, stage); break;
     default:
       if constexpr (kVec > 4) {
         switch (r) {
-          case 4: store_window<T, (kVec > 4 ? 4 : 0)>(base, q, v, lane); break;
-          case 5: store_window<T, (kVec > 4 ? 5 : 0)>(base, q, v, lane); break;
-          case 6: store_window<T, (kVec > 4 ? 6 : 0)>(base, q, v, lane); break;
-          default: store_window<T, (kVec > 4 ? 7 : 0)>(base, q, v, lane); break;
+          case 4: store_window<T, (kVec > 4 ? 4 : 0)>(base, q, v, lane, stage); break;
+          case 5: store_window<T, (kVec > 4 ? 5 : 0)>(base, q, v, lane, stage); break;
+          case 6: store_window<T, (kVec > 4 ? 6 : 0)>(base, q, v, lane, stage); break;
+          default: store_window<T, (kVec > 4 ? 7 : 0)>(base, q, v, lane, stage); break;
         }
       }
       break;
