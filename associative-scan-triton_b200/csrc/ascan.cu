@@ -1422,16 +1422,19 @@ static int g_tile_width = 0;
 // per-tile chain (fold, warp scan, hand-offs, carry) per byte.  Measured on
 // B200 (fwd / bwd, us): B=8, C=1536, fp32 T=4096 fwd 143 -> 106, T=65536
 // 2267 -> 1481; bf16 T=4096 139/173 -> 99/130; fp16 T=2048 76/92 -> 55/69;
-// C=256, T=2^20 fwd 868 -> 559.  They lose in ragged forward rows (C=257,
-// T=100003: 119 -> 201), when they would turn a row order into a flat one
-// for the forward (varlen C=2048: 1150 -> 1196), and gain nothing when the
-// tiles are too few to fill the SMs twice.  Rows fewer than the CTAs would
-// put a tile's predecessor in its own wave.
+// C=256, T=2^20 fwd 868 -> 559; 16-bit varlen rows (bf16, C=2048) fwd
+// 1127 -> 800.  They lose when they would turn a row order into a flat one
+// for the fp32 forward (varlen C=2048: 1150 -> 1196), and gain nothing when
+// the tiles are too few to fill the SMs twice.  Rows fewer than the CTAs
+// would put a tile's predecessor in its own wave.
 static bool use_wide(int64_t N, int64_t BL, int64_t S, bool allow_ragged, bool forward,
                      bool narrow_type = false, bool* row_hint = nullptr) {
   if (row_hint) *row_hint = false;
-  if (g_tile_width != 0) return g_tile_width == 32;
   tma::TileSched wide = make_sched(tma::Geo<32>::kTileElems, N, BL, S, allow_ragged);
+  // fp32 ragged rows at the wide width would need a 257-row TMA box, one
+  // more than a box may hold: those launches keep the narrow tiles
+  const bool box_ok = !forward || narrow_type || !wide.ragged;
+  if (g_tile_width != 0) return g_tile_width == 32 && box_ok;
   if (forward) {
     // keep the narrow row order unless sequences average a whole wide tile
     // (then the wide flat tiles mostly start at sequence heads); 16-bit
@@ -1443,9 +1446,7 @@ static bool use_wide(int64_t N, int64_t BL, int64_t S, bool allow_ragged, bool f
       if (!wide.row_mode) return false;
       *row_hint = true;
     }
-    // fp32 ragged rows at the wide width store 128 bytes per lane from
-    // registers, which measured slower than the narrow tiles
-    if (wide.ragged && !narrow_type) return false;
+    if (!box_ok) return false;
   }
   const uint32_t sms = static_cast<uint32_t>(sm_count());
   if (sms == 0 || wide.num_tiles < 2 * sms) return false;

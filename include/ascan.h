@@ -279,7 +279,8 @@ ASCAN_API int ascan_get_implementation(void);
  * counterpart in the reference): 0 (default) chooses per launch, 16 or 32
  * forces 4096- or 8192-element tiles (16 or 32 elements per consumer
  * thread) wherever the library has both kernels -- the forward of every
- * dtype without gates_out, and the backward of fp16/bf16 (time slabs
+ * dtype without gates_out (fp32 ragged rows excepted: their shifted load
+ * would exceed a TMA box), and the backward of fp16/bf16 (time slabs
  * included); other launches always use 16.  Process-wide; results agree up
  * to rounding.
  */
