@@ -1,7 +1,7 @@
 """GPU: the dispatcher-level ops inside CUDA graphs.
 
-The launch-bound small-T regime (SURVEY's small-T overhead item; the
-reference loses to warpscan at T <= 256 on host overhead) is served by
+The launch-bound small-T regime (where the reference loses to a hand-written
+warp scan at T <= 256 on host overhead, reference README.md:99-110) is served by
 capturing the forward and backward calls once and replaying the graph: the
 workspace comes from the graph's memory pool, the status clear and the kernel
 launches are captured stream operations, and the persistent kernels'
