@@ -1,16 +1,20 @@
 """ctypes binding of the native library ``libascan_b200.so`` (C ABI: include/ascan.h).
 
 Every op of this package reaches the GPU through the entry points bound here --
-``ascan_forward``, ``ascan_backward``, ``ascan_shift_pad`` and, for time
-slabs, ``ascan_forward_slab`` / ``ascan_backward_slab`` -- with raw device
-pointers, sizes and torch's current CUDA stream.  There is no CPU
+``ascan_forward``, ``ascan_backward``, ``ascan_shift_pad``, the bidirectional
+pairs and, for time slabs, ``ascan_forward_slab`` / ``ascan_backward_slab`` /
+``ascan_time_shard_fold`` -- with raw device pointers, sizes and torch's
+current CUDA stream.  There is no CPU
 path: a missing library, a CPU tensor or a machine without CUDA raises.
 
 Device-side checks (malformed ``cu_seqlens``, a look-back that gave up) set a
-sticky error word on the device.  Reading it needs a device synchronisation,
-so it is only read when sync checking is on (``set_sync_check(True)`` or the
-environment variable ``ASCAN_SYNC_CHECK=1``) or when :func:`check_device_error`
-is called.
+sticky error word on the device and a pinned host word (``ascan_error_flag``,
+enabled by the first op).  After every op the host word is read -- a plain
+memory read, no synchronisation -- and a set flag raises :class:`ScanError`
+(with the exact bits, read after a synchronisation) from that op or a later
+one, once the failing kernel has run.  With sync checking on
+(``set_sync_check(True)`` or ``ASCAN_SYNC_CHECK=1``) every op synchronises and
+reports its own error; :func:`check_device_error` does the same on demand.
 """
 
 from __future__ import annotations
@@ -44,6 +48,7 @@ EXPORTED_SYMBOLS = (
   "ascan_backward",
   "ascan_forward_slab",
   "ascan_backward_slab",
+  "ascan_time_shard_fold",
   "ascan_workspace_size_bidi",
   "ascan_forward_bidi",
   "ascan_backward_bidi",
@@ -54,6 +59,7 @@ EXPORTED_SYMBOLS = (
   "ascan_get_tile_width",
   "ascan_get_device_error",
   "ascan_clear_device_error",
+  "ascan_error_flag",
   "ascan_selftest_waits",
 )
 
@@ -67,6 +73,7 @@ class ScanError(RuntimeError):
 _lib = None
 _load_error: Exception | None = None
 _sync_check = os.environ.get("ASCAN_SYNC_CHECK", "0") not in ("", "0")
+_flag: ctypes.c_uint | None = None  # the library's pinned host error flag, once enabled
 
 
 def _bind(lib) -> None:
@@ -88,6 +95,9 @@ def _bind(lib) -> None:
   lib.ascan_backward_slab.restype = ci
   lib.ascan_backward_slab.argtypes = [p, p, p, p, p, p, ci, i64, i64, i64, ci, ci, p, p, p, p,
                                       sz, p]
+  lib.ascan_time_shard_fold.restype = ci
+  lib.ascan_time_shard_fold.argtypes = [p, i64, ci, ci, i64, ctypes.c_uint32, ctypes.c_uint32, ci,
+                                        p, p, p]
   lib.ascan_workspace_size_bidi.restype = sz
   lib.ascan_workspace_size_bidi.argtypes = [i64, i64, ci]
   lib.ascan_forward_bidi.restype = ci
@@ -110,6 +120,8 @@ def _bind(lib) -> None:
                                          ctypes.POINTER(ctypes.c_longlong)]
   lib.ascan_clear_device_error.restype = ci
   lib.ascan_clear_device_error.argtypes = [ci]
+  lib.ascan_error_flag.restype = p
+  lib.ascan_error_flag.argtypes = []
   lib.ascan_selftest_waits.restype = ci
   lib.ascan_selftest_waits.argtypes = [p, sz, ctypes.c_longlong,
                                        ctypes.POINTER(ctypes.c_longlong), p]
@@ -271,10 +283,27 @@ def _stream_ptr(device: torch.device) -> int:
   return torch.cuda.current_stream(device).cuda_stream
 
 
+def _enable_error_flag() -> None:
+  """Enable the library's pinned host error flag (once, outside any stream
+  capture: its first use allocates pinned host memory)."""
+  global _flag
+  if _flag is None and not torch.cuda.is_current_stream_capturing():
+    ptr = load().ascan_error_flag()
+    if ptr:
+      _flag = ctypes.c_uint.from_address(ptr)
+
+
+def error_flag() -> int:
+  """The host error flag's current bits (0: no device error seen yet), read
+  without synchronising."""
+  _enable_error_flag()
+  return int(_flag.value) if _flag is not None else 0
+
+
 def _finish(rc: int, what: str, device: torch.device) -> None:
   if rc != ASCAN_OK:
     raise ScanError(f"{what}: {strerror(rc)}")
-  if _sync_check:
+  if _sync_check or (_flag is not None and _flag.value):
     check_device_error(device)
 
 
@@ -296,6 +325,7 @@ def _check_inputs(names_tensors, cu_seqlens, num_seq):
     raise ValueError("cu_seqlens must be contiguous")
   if cu_seqlens.numel() != num_seq + 1:
     raise ValueError(f"cu_seqlens has {cu_seqlens.numel()} entries, expected {num_seq + 1}")
+  _enable_error_flag()  # the inputs are CUDA tensors: a device exists
   return device
 
 
@@ -485,6 +515,27 @@ def backward_slab(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
       cu_seqlens.data_ptr(), INDEX_CODES[cu_seqlens.dtype], int(num_seq), C, BL, dcode,
       int(bool(causal)), carry, halo, agg, ws.data_ptr(), ws.numel(), _stream_ptr(device))
   _finish(rc, "ascan_backward_slab", device)
+
+
+def time_shard_fold(records: torch.Tensor, world: int, rank: int, num_channels: int,
+                    starts_new_mask: int, inner_boundary_mask: int, direction: int,
+                    carry_out: torch.Tensor, halo_out: torch.Tensor | None = None) -> None:
+  """ascan_time_shard_fold: the carry entering slab ``rank`` from the gathered
+  records ``[world, record_floats]`` (float32, contiguous, CUDA)."""
+  _require_cuda("records", records, None)
+  device = records.device
+  if records.dtype != torch.float32 or not records.is_contiguous() or records.dim() != 2 \
+      or records.shape[0] != world:
+    raise ValueError(f"records must be a contiguous float32 [{world}, k] tensor")
+  C = int(num_channels)
+  carry = _row_array("carry_out", carry_out, C, 2 if direction == 0 else 1, device)
+  halo = _row_array("halo_out", halo_out, C, 1, device)
+  with torch.cuda.device(device):
+    rc = load().ascan_time_shard_fold(
+      records.data_ptr(), int(records.shape[1]), int(world), int(rank), C,
+      int(starts_new_mask), int(inner_boundary_mask), int(direction), carry, halo,
+      _stream_ptr(device))
+  _finish(rc, "ascan_time_shard_fold", device)
 
 
 def shift_pad(data: torch.Tensor, out: torch.Tensor, cu_seqlens: torch.Tensor,

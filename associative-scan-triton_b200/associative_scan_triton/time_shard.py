@@ -11,13 +11,15 @@ forward (``h[t] = g[t] h[t-1] + x[t]``)
      writing outputs and keeps, per row, the gate product ``P`` and the state
      ``Y`` at its last column (``ascan_forward_slab`` with ``tokens_out=NULL``);
   2. exchange: one all-gather of ``[C, 2]`` floats per rank (NCCL over
-     NVLink);
+     NVLink) into a preallocated ``[W, 2C]`` buffer;
   3. each rank folds the records of the ranks before it into its carry
-     ``(product, state)`` (:func:`forward_carry`);
+     ``(product, state)`` with one small kernel (``ascan_time_shard_fold``;
+     :func:`forward_carry` is the same fold on the host);
   4. seeded pass: the slab's forward with that carry entering each row's
      first column (``ascan_forward_slab`` with ``row_carry``).
-  Traffic: 2 reads in pass 1, 2 reads + 1 write in pass 2 (5 element
-  transfers against 3 for a single-device scan).
+  Pass 1 is a row reduction over the slab's last sequence piece (no scan, no
+  stores).  Traffic: 2 reads in pass 1, 2 reads + 1 write in pass 2 (5
+  element transfers against 3 for a single-device scan).
 
 backward (``dh[t] = dy[t] + g[t+1] dh[t+1]``, ``dg[t] = dh[t] h[t-1]``)
   mirrored from the last rank to the first; the exchange also carries each
@@ -29,10 +31,12 @@ channel, as in the reference's packed layout); :func:`plan_slabs` rebases them
 to each slab and records whether the slab's first piece continues a sequence
 from the previous slab and whether a boundary lies inside it.  The carry
 folds need only those flags and the exchanged per-row records, so they are
-the same code for the multi-process driver (:func:`scan_causal_time_sharded`,
-:class:`ScanCausalTimeShard`), for single-process emulation of all slabs on
-one GPU (:func:`emulate_forward`, :func:`emulate_backward`) and for the CPU
-protocol tests.
+the same code for the multi-process driver (:class:`TimeShardStep`,
+:func:`scan_causal_time_sharded`, :class:`ScanCausalTimeShard`), for
+single-process emulation of all slabs on one GPU (:func:`emulate_forward`,
+:func:`emulate_backward`) and, restated on the host
+(:func:`forward_carry`, :func:`backward_carry`, :func:`state_halo`), for the
+CPU protocol tests.
 """
 
 from __future__ import annotations
@@ -47,7 +51,8 @@ from . import _lib
 __all__ = [
   "SlabPlan", "plan_slabs", "even_bounds", "forward_carry", "backward_carry",
   "slab_forward_aggregate", "slab_forward", "slab_backward_aggregate", "slab_backward",
-  "emulate_forward", "emulate_backward", "scan_causal_time_sharded", "ScanCausalTimeShard",
+  "emulate_forward", "emulate_backward", "plan_masks", "fold_forward", "fold_backward",
+  "TimeShardStep", "scan_causal_time_sharded", "ScanCausalTimeShard",
 ]
 
 
@@ -150,6 +155,41 @@ def state_halo(plans: Sequence[SlabPlan], last_states: Sequence[torch.Tensor],
   return last_states[rank - 1].float().contiguous()
 
 
+def plan_masks(plans: Sequence[SlabPlan]) -> tuple[int, int]:
+  """(starts_new, inner_boundary) bit masks over the slabs (at most 32)."""
+  if len(plans) > 32:
+    raise ValueError("at most 32 slabs")
+  starts = sum(1 << j for j, p in enumerate(plans) if p.starts_new)
+  inner = sum(1 << j for j, p in enumerate(plans) if p.inner_boundary)
+  return starts, inner
+
+
+def fold_forward(records: torch.Tensor, plans: Sequence[SlabPlan], rank: int,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+  """:func:`forward_carry` on the device: ``records`` ``[W, >= 2C]`` float32
+  holds every slab's (P, Y) row aggregate interleaved in its first 2C floats."""
+  C = records.shape[1] // 2 if out is None else out.shape[0]
+  carry = torch.empty(C, 2, dtype=torch.float32, device=records.device) if out is None else out
+  starts, inner = plan_masks(plans)
+  _lib.time_shard_fold(records, len(plans), rank, C, starts, inner, 0, carry)
+  return carry
+
+
+def fold_backward(records: torch.Tensor, plans: Sequence[SlabPlan], rank: int,
+                  carry_out: torch.Tensor | None = None,
+                  halo_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+  """:func:`backward_carry` and :func:`state_halo` on the device: record j of
+  ``records`` ``[W, 4C]`` is slab j's (Q, D) aggregate (2C floats), first gate
+  column (C) and last state column (C)."""
+  C = records.shape[1] // 4
+  dev = records.device
+  carry = torch.empty(C, dtype=torch.float32, device=dev) if carry_out is None else carry_out
+  halo = torch.empty(C, dtype=torch.float32, device=dev) if halo_out is None else halo_out
+  starts, inner = plan_masks(plans)
+  _lib.time_shard_fold(records, len(plans), rank, C, starts, inner, 1, carry, halo)
+  return carry, halo
+
+
 # ---------------------------------------------------------------------------
 # per-slab passes (one GPU, one slab)
 # ---------------------------------------------------------------------------
@@ -171,10 +211,10 @@ def _cu_tensor(plan: SlabPlan, device) -> torch.Tensor:
 
 
 def slab_forward_aggregate(gates: torch.Tensor, tokens: torch.Tensor,
-                           plan: SlabPlan) -> torch.Tensor:
+                           plan: SlabPlan, out: torch.Tensor | None = None) -> torch.Tensor:
   """Pass 1 of the forward: (P, Y) ``[C, 2]`` of the slab from a zero state."""
   C = gates.shape[0]
-  agg = torch.empty(C, 2, dtype=torch.float32, device=gates.device)
+  agg = torch.empty(C, 2, dtype=torch.float32, device=gates.device) if out is None else out
   cu = _cu_tensor(plan, gates.device)
   _lib.forward_slab(gates, tokens, None, None, cu, cu.numel() - 1, C, False,
                     row_aggregate=agg)
@@ -194,12 +234,14 @@ def slab_forward(gates: torch.Tensor, tokens: torch.Tensor, plan: SlabPlan,
 
 
 def slab_backward_aggregate(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
-                            plan: SlabPlan) -> torch.Tensor:
+                            plan: SlabPlan, out: torch.Tensor | None = None,
+                            zero: torch.Tensor | None = None) -> torch.Tensor:
   """Pass 1 of the backward: (Q, D) ``[C, 2]`` at the slab's first column from
   a zero carry at its last column."""
   C = gates.shape[0]
-  agg = torch.empty(C, 2, dtype=torch.float32, device=gates.device)
-  zero = torch.zeros(C, dtype=torch.float32, device=gates.device)
+  agg = torch.empty(C, 2, dtype=torch.float32, device=gates.device) if out is None else out
+  if zero is None:
+    zero = torch.zeros(C, dtype=torch.float32, device=gates.device)
   cu = _cu_tensor(plan, gates.device)
   _lib.backward_slab(grad, gates, states, None, None, cu, cu.numel() - 1, C, True,
                      row_carry=zero, row_aggregate=agg)
@@ -207,12 +249,13 @@ def slab_backward_aggregate(grad: torch.Tensor, gates: torch.Tensor, states: tor
 
 
 def slab_backward(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
-                  plan: SlabPlan, carry: torch.Tensor,
-                  halo: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+                  plan: SlabPlan, carry: torch.Tensor, halo: torch.Tensor,
+                  d_gates: torch.Tensor | None = None,
+                  d_tokens: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
   """Pass 2 of the backward: (d_gates, d_tokens) of the slab."""
   C = gates.shape[0]
-  dx = torch.empty_like(grad)
-  dg = torch.empty_like(gates)
+  dx = torch.empty_like(grad) if d_tokens is None else d_tokens
+  dg = torch.empty_like(gates) if d_gates is None else d_gates
   cu = _cu_tensor(plan, gates.device)
   _lib.backward_slab(grad, gates, states, dx, dg, cu, cu.numel() - 1, C, True,
                      row_carry=carry, row_state_halo=halo)
@@ -225,10 +268,14 @@ def slab_backward(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
 
 def emulate_forward(gates: Sequence[torch.Tensor], tokens: Sequence[torch.Tensor],
                     plans: Sequence[SlabPlan]) -> list[torch.Tensor]:
-  """The time-sharded forward of all slabs in one process (same passes and
-  folds as the distributed driver; the exchange is a Python list)."""
-  aggs = [slab_forward_aggregate(g, x, p) for g, x, p in zip(gates, tokens, plans)]
-  return [slab_forward(g, x, p, forward_carry(plans, aggs, k))
+  """The time-sharded forward of all slabs in one process: the same passes
+  and device fold as the distributed driver; the exchange is writing every
+  slab's record into one ``[W, 2C]`` buffer."""
+  C, W = gates[0].shape[0], len(plans)
+  records = torch.empty(W, 2 * C, dtype=torch.float32, device=gates[0].device)
+  for k, (g, x, p) in enumerate(zip(gates, tokens, plans)):
+    slab_forward_aggregate(g, x, p, out=records[k].view(C, 2))
+  return [slab_forward(g, x, p, fold_forward(records, plans, k))
           for k, (g, x, p) in enumerate(zip(gates, tokens, plans))]
 
 
@@ -236,12 +283,18 @@ def emulate_backward(grads: Sequence[torch.Tensor], gates: Sequence[torch.Tensor
                      states: Sequence[torch.Tensor],
                      plans: Sequence[SlabPlan]) -> list[tuple[torch.Tensor, torch.Tensor]]:
   """The time-sharded backward of all slabs in one process."""
-  aggs = [slab_backward_aggregate(dy, g, h, p) for dy, g, h, p in zip(grads, gates, states, plans)]
-  firsts = [g[:, 0].float().contiguous() for g in gates]
-  lasts = [h[:, -1].float().contiguous() for h in states]
-  return [slab_backward(dy, g, h, p, backward_carry(plans, aggs, firsts, k),
-                        state_halo(plans, lasts, k))
-          for k, (dy, g, h, p) in enumerate(zip(grads, gates, states, plans))]
+  C, W = gates[0].shape[0], len(plans)
+  records = torch.empty(W, 4 * C, dtype=torch.float32, device=gates[0].device)
+  zero = torch.zeros(C, dtype=torch.float32, device=gates[0].device)
+  for k, (dy, g, h, p) in enumerate(zip(grads, gates, states, plans)):
+    slab_backward_aggregate(dy, g, h, p, out=records[k, :2 * C].view(C, 2), zero=zero)
+    records[k, 2 * C:3 * C].copy_(g[:, 0])
+    records[k, 3 * C:].copy_(h[:, -1])
+  out = []
+  for k, (dy, g, h, p) in enumerate(zip(grads, gates, states, plans)):
+    carry, halo = fold_backward(records, plans, k)
+    out.append(slab_backward(dy, g, h, p, carry, halo))
+  return out
 
 
 # ---------------------------------------------------------------------------
@@ -264,9 +317,112 @@ def _rank_plans(cu_seqlens, bounds) -> list[SlabPlan]:
   return plan_slabs(cu, bounds)
 
 
+class TimeShardStep:
+  """One rank's slab of a time-sharded causal scan, forward and backward,
+  with every buffer allocated once: the records, their all-gather targets,
+  the carries and (unless the caller passes its own) the outputs.
+
+  forward:  row reduction -> all-gather of [2C] floats -> device fold ->
+            seeded forward slab pass;
+  backward: row reduction + first gate / last state columns -> all-gather
+            of [4C] floats -> device fold -> seeded fused backward slab pass.
+  Six kernels and two collectives per fwd+bwd, no host synchronisation, so a
+  step can be captured in a CUDA graph.  ``gather(out, inp)`` defaults to
+  ``torch.distributed.all_gather_into_tensor`` on ``group``."""
+
+  def __init__(self, shape, dtype, plans: Sequence[SlabPlan], rank: int, device,
+               group=None, gather: Callable[[torch.Tensor, torch.Tensor], None] | None = None,
+               allocate_outputs: bool = True):
+    C, L = (int(v) for v in shape)
+    self.C, self.L, self.rank, self.world = C, L, rank, len(plans)
+    self.plans, self.plan = list(plans), plans[rank]
+    if self.plan.length != L:
+      raise ValueError(f"slab {rank} has {self.plan.length} columns, tensors have {L}")
+    device = torch.device(device)
+    self.cu = _cu_tensor(self.plan, device)
+    self.num_seq = self.cu.numel() - 1
+    f32 = dict(dtype=torch.float32, device=device)
+    self.rec_f = torch.empty(2 * C, **f32)
+    self.all_f = torch.empty(self.world, 2 * C, **f32)
+    self.rec_b = torch.empty(4 * C, **f32)
+    self.all_b = torch.empty(self.world, 4 * C, **f32)
+    self.carry_f = torch.empty(C, 2, **f32)
+    self.carry_b = torch.empty(C, **f32)
+    self.halo = torch.empty(C, **f32)
+    self.zero = torch.zeros(C, **f32)
+    self.masks = plan_masks(plans)
+    self.y = self.dx = self.dg = None
+    if allocate_outputs:
+      self.y = torch.empty(C, L, dtype=dtype, device=device)
+      self.dx = torch.empty(C, L, dtype=dtype, device=device)
+      self.dg = torch.empty(C, L, dtype=dtype, device=device)
+    if gather is None:
+      import torch.distributed as dist
+
+      def gather(out, inp):
+        dist.all_gather_into_tensor(out, inp, group=group)
+    self._gather = gather
+
+  @staticmethod
+  def _mark(marks):
+    if marks is not None:
+      ev = torch.cuda.Event(enable_timing=True)
+      ev.record()
+      marks.append(ev)
+
+  def forward(self, gates: torch.Tensor, tokens: torch.Tensor,
+              out: torch.Tensor | None = None, marks: list | None = None) -> torch.Tensor:
+    """``marks``: if a list, a timing event is recorded after each phase
+    (aggregate, exchange, fold, seeded pass)."""
+    C, cu, S = self.C, self.cu, self.num_seq
+    y = self.y if out is None else out
+    if y is None:
+      y = torch.empty_like(tokens)
+    _lib.forward_slab(gates, tokens, None, None, cu, S, C, False,
+                      row_aggregate=self.rec_f.view(C, 2))
+    self._mark(marks)
+    self._gather(self.all_f, self.rec_f)
+    self._mark(marks)
+    starts, inner = self.masks
+    _lib.time_shard_fold(self.all_f, self.world, self.rank, C, starts, inner, 0, self.carry_f)
+    self._mark(marks)
+    _lib.forward_slab(gates, tokens, y, None, cu, S, C, False, row_carry=self.carry_f)
+    self._mark(marks)
+    return y
+
+  def backward(self, grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
+               d_gates: torch.Tensor | None = None, d_tokens: torch.Tensor | None = None,
+               marks: list | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``marks``: as in :meth:`forward` (aggregate + edge columns, exchange,
+    fold, seeded pass)."""
+    C, cu, S = self.C, self.cu, self.num_seq
+    dg = self.dg if d_gates is None else d_gates
+    dx = self.dx if d_tokens is None else d_tokens
+    if dg is None:
+      dg = torch.empty_like(gates)
+    if dx is None:
+      dx = torch.empty_like(grad)
+    _lib.backward_slab(grad, gates, states, None, None, cu, S, C, True, row_carry=self.zero,
+                       row_aggregate=self.rec_b[:2 * C].view(C, 2))
+    self.rec_b[2 * C:3 * C].copy_(gates[:, 0])
+    self.rec_b[3 * C:].copy_(states[:, -1])
+    self._mark(marks)
+    self._gather(self.all_b, self.rec_b)
+    self._mark(marks)
+    starts, inner = self.masks
+    _lib.time_shard_fold(self.all_b, self.world, self.rank, C, starts, inner, 1, self.carry_b,
+                         self.halo)
+    self._mark(marks)
+    _lib.backward_slab(grad, gates, states, dx, dg, cu, S, C, True, row_carry=self.carry_b,
+                       row_state_halo=self.halo)
+    self._mark(marks)
+    return dg, dx
+
+
 def time_sharded_forward(gates: torch.Tensor, tokens: torch.Tensor, plans: Sequence[SlabPlan],
                          rank: int, gather: Callable[[torch.Tensor], list[torch.Tensor]]):
-  """Forward of this rank's slab: aggregate, exchange, seeded scan."""
+  """Forward of this rank's slab with a list-returning gather (host folds):
+  aggregate, exchange, seeded scan."""
   agg = slab_forward_aggregate(gates, tokens, plans[rank])
   aggs = gather(agg)
   return slab_forward(gates, tokens, plans[rank], forward_carry(plans, aggs, rank))
@@ -275,8 +431,9 @@ def time_sharded_forward(gates: torch.Tensor, tokens: torch.Tensor, plans: Seque
 def time_sharded_backward(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
                           plans: Sequence[SlabPlan], rank: int,
                           gather: Callable[[torch.Tensor], list[torch.Tensor]]):
-  """Backward of this rank's slab: aggregate, one exchange of
-  (Q, D, first gate, last state) per row, seeded fused backward."""
+  """Backward of this rank's slab with a list-returning gather (host folds):
+  aggregate, one exchange of (Q, D, first gate, last state) per row, seeded
+  fused backward."""
   agg = slab_backward_aggregate(grad, gates, states, plans[rank])
   packed = torch.cat([agg, gates[:, :1].float(), states[:, -1:].float()], dim=1)
   recs = gather(packed)
@@ -297,17 +454,17 @@ class ScanCausalTimeShard(torch.autograd.Function):
     import torch.distributed as dist
     plans = _rank_plans(cu_seqlens, bounds)
     rank = dist.get_rank(group)
-    gather = lambda t: _all_gather(t, group)  # noqa: E731
-    out = time_sharded_forward(gates, tokens, plans, rank, gather)
+    step = TimeShardStep(gates.shape, gates.dtype, plans, rank, gates.device, group=group,
+                         allocate_outputs=False)
+    out = step.forward(gates, tokens)
     ctx.save_for_backward(out, gates)
-    ctx.plans, ctx.rank, ctx.group = plans, rank, group
+    ctx.step = step
     return out
 
   @staticmethod
   def backward(ctx, grad):
     out, gates = ctx.saved_tensors
-    gather = lambda t: _all_gather(t, ctx.group)  # noqa: E731
-    dg, dx = time_sharded_backward(grad.contiguous(), gates, out, ctx.plans, ctx.rank, gather)
+    dg, dx = ctx.step.backward(grad.contiguous(), gates, out)
     return dg, dx, None, None, None
 
 

@@ -11,6 +11,8 @@ namespace ascan {
 // Process-wide switches (ascan_set_implementation / ascan_set_tile_width).
 int g_impl = -1;
 int g_tile_width = 0;
+uint32_t* g_err_host = nullptr;
+static uint32_t* g_err_host_ptr = nullptr;  // host address of the same word
 
 // Fixed scratch of ascan_forward_noalloc: the look-back workspace for callers
 // that cannot allocate device memory.  Every device that loads this library
@@ -19,6 +21,9 @@ constexpr size_t kNoAllocScratchBytes = ASCAN_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 int selftest_waits_run(void* workspace, long long limit_ns, long long* results, cudaStream_t s);
+int time_shard_fold_run(const float* records, int64_t record_floats, int world, int rank,
+                        int64_t C, uint32_t new_mask, uint32_t inner_mask, int direction,
+                        float* carry, float* halo, cudaStream_t s);
 
 }  // namespace ascan
 
@@ -167,6 +172,20 @@ int ascan_backward_slab(const void* grad, const void* gates, const void* states,
                   seq_total, causal, w, s, io)
   ASCAN_DISPATCH_TYPES(dtype, cu_index_type, ASCAN_BWD_CALL);
 #undef ASCAN_BWD_CALL
+}
+
+int ascan_time_shard_fold(const float* records, int64_t record_floats, int world, int rank,
+                          int64_t num_channels, uint32_t starts_new_mask,
+                          uint32_t inner_boundary_mask, int direction, float* carry_out,
+                          float* halo_out, void* stream) {
+  if (!records || !carry_out || world < 1 || world > 32 || rank < 0 || rank >= world ||
+      num_channels <= 0 || (direction != 0 && direction != 1))
+    return ASCAN_EINVAL;
+  if (record_floats < (direction == 0 ? 2 : 4) * num_channels) return ASCAN_EINVAL;
+  if (direction == 0 && halo_out) return ASCAN_EINVAL;
+  return time_shard_fold_run(records, record_floats, world, rank, num_channels, starts_new_mask,
+                             inner_boundary_mask, direction, carry_out, halo_out,
+                             static_cast<cudaStream_t>(stream));
 }
 
 // Workspace of a bidirectional pair: two halves, one per scan, each a
@@ -422,6 +441,27 @@ int ascan_selftest_waits(void* workspace, size_t workspace_bytes, long long limi
   return selftest_waits_run(workspace, limit_ns, results, static_cast<cudaStream_t>(stream));
 }
 
+volatile unsigned int* ascan_error_flag(void) {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = nullptr;
+    if (cudaHostAlloc(&h, 64, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      return;
+    }
+    memset(h, 0, 64);
+    void* d = nullptr;
+    if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess || d == nullptr) {
+      cudaGetLastError();
+      cudaFreeHost(h);
+      return;
+    }
+    g_err_host_ptr = static_cast<uint32_t*>(h);
+    g_err_host = static_cast<uint32_t*>(d);  // kernels launched from now on write it
+  });
+  return g_err_host_ptr;
+}
+
 int ascan_clear_device_error(int device) {
   int prev = -1;
   if (cudaGetDevice(&prev) != cudaSuccess) return ASCAN_EDEVICE;
@@ -431,6 +471,7 @@ int ascan_clear_device_error(int device) {
   if (rc == ASCAN_OK) rc = unit_err_##NAME(1, nullptr, nullptr);
   ASCAN_UNITS(ASCAN_CLEAR_UNIT)
 #undef ASCAN_CLEAR_UNIT
+  if (g_err_host_ptr) *reinterpret_cast<volatile uint32_t*>(g_err_host_ptr) = 0u;
   cudaSetDevice(prev);
   return rc;
 }

@@ -54,14 +54,21 @@ namespace ascan {
 static __device__ unsigned int g_err_code = 0;
 static __device__ unsigned long long g_err_detail = 0;
 
-__device__ __forceinline__ void report(unsigned int bits, unsigned long long detail) {
+// Records an error in this unit's sticky word and, when the process enabled
+// one (ascan_error_flag), in the pinned host word the host polls without
+// synchronising (a plain store: concurrent reports may overwrite each other's
+// bits there; the sticky word keeps all of them).
+__device__ __forceinline__ void report(unsigned int bits, unsigned long long detail,
+                                       uint32_t* host) {
   if (atomicOr(&g_err_code, bits) == 0u) atomicExch(&g_err_detail, detail);
+  if (host) asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(host), "r"(bits) : "memory");
 }
 
 // The first tile checks cu_seqlens once per launch.  Every other tile only
 // clamps what it reads (cu_at), so a bad array can never move an access.
 template <typename IdxT>
-__device__ void validate_cu(const IdxT* __restrict__ cu, int64_t S, int64_t BL) {
+__device__ void validate_cu(const IdxT* __restrict__ cu, int64_t S, int64_t BL,
+                            uint32_t* err_host) {
   unsigned bits = 0u;
   for (int64_t i = threadIdx.x; i <= S; i += kThreads) {
     const int64_t v = static_cast<int64_t>(__ldg(cu + i));
@@ -69,7 +76,7 @@ __device__ void validate_cu(const IdxT* __restrict__ cu, int64_t S, int64_t BL) 
     if (i < S && static_cast<int64_t>(__ldg(cu + i + 1)) < v) bits |= ASCAN_DEV_ERR_CU_ORDER;
     if (i == S && v != BL) bits |= ASCAN_DEV_ERR_CU_END;
   }
-  if (bits) report(bits, 0ull);
+  if (bits) report(bits, 0ull, err_host);
 }
 
 // Tile-level tail shared by the forward and backward kernels: chains the warp
@@ -78,7 +85,8 @@ __device__ void validate_cu(const IdxT* __restrict__ cu, int64_t S, int64_t BL) 
 // this warp's first element in scan order.
 template <bool REV>
 __device__ __forceinline__ Pfx tile_prefix(Pfx warp_total, bool first_is_head, uint32_t ticket,
-                                           const TileStatus& st, int warp, int lane) {
+                                           const TileStatus& st, int warp, int lane,
+                                           uint32_t* err_host) {
   __shared__ Pfx s_warp[kWarps];
   __shared__ int s_first_head;
   __shared__ Pfx s_te;
@@ -105,7 +113,7 @@ __device__ __forceinline__ Pfx tile_prefix(Pfx warp_total, bool first_is_head, u
     if (need_lookback) {
       bool timed_out = false;
       te = lookback_warp<kLookbackPerLane>(st, ticket, lane, &timed_out);
-      if (timed_out && lane == 0) report(ASCAN_DEV_ERR_LOOKBACK, ticket);
+      if (timed_out && lane == 0) report(ASCAN_DEV_ERR_LOOKBACK, ticket, err_host);
       if (lane == 0) {
         if (!(tot.f & kHead)) {
           const Pfx inc = compose(te, tot);
@@ -160,7 +168,8 @@ __device__ __forceinline__ int64_t row_pos(int64_t p, int64_t BL, bool small) {
 }
 
 template <typename T, typename IdxT, int VEC, bool REV, bool GATES_OUT>
-__global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdArgs<T, IdxT> args) {
+__global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdArgs<T, IdxT> args,
+                                                            uint32_t* err_host) {
   constexpr int R = kElemsPerThread / VEC;
   constexpr int kRowElems = 32 * VEC;
   constexpr int kWarpElems = R * kRowElems;
@@ -182,7 +191,7 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdArgs<T, Idx
     load_vec<T, VEC>(args.g, p, N, 1.f, ga[r]);
     load_vec<T, VEC>(args.x, p, N, 0.f, xb[r]);
   }
-  if (ticket == 0) validate_cu(args.cu, S, BL);
+  if (ticket == 0) validate_cu(args.cu, S, BL, err_host);
 
   // Sequence boundaries of every element this lane owns.
   unsigned head[R], wmask[R];
@@ -213,7 +222,7 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdArgs<T, Idx
     carry = compose(carry, tot);
   }
   const bool first_is_head = (head[REV ? R - 1 : 0] >> (REV ? VEC - 1 : 0)) & 1u;
-  const Pfx wpre = tile_prefix<REV>(carry, first_is_head, ticket, args.st, warp, lane);
+  const Pfx wpre = tile_prefix<REV>(carry, first_is_head, ticket, args.st, warp, lane, err_host);
 
   // Final recurrence from the exact carry-in of each vector.
 #pragma unroll
@@ -281,7 +290,8 @@ __device__ __forceinline__ void prev_last(const float (&last)[R], float edge, in
 // CAUSAL: adjoint of the causal scan, dh[t] = dy[t] + g[t+1] dh[t+1] (scan
 // runs right to left), dg[t] = dh[t] h[t-1].  !CAUSAL mirrors both shifts.
 template <typename T, typename IdxT, int VEC, bool CAUSAL>
-__global__ void __launch_bounds__(kThreads) scan_bwd_kernel(const BwdArgs<T, IdxT> args) {
+__global__ void __launch_bounds__(kThreads) scan_bwd_kernel(const BwdArgs<T, IdxT> args,
+                                                            uint32_t* err_host) {
   constexpr bool REV = CAUSAL;
   constexpr int R = kElemsPerThread / VEC;
   constexpr int kRowElems = 32 * VEC;
@@ -316,7 +326,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_kernel(const BwdArgs<T, Idx
     if (lane == 0 && pp >= 0) g_edge = Cvt<T>::to(args.g[pp]);
     if (lane == 31 && pn < N) h_edge = Cvt<T>::to(args.h[pn]);
   }
-  if (ticket == 0) validate_cu(args.cu, S, BL);
+  if (ticket == 0) validate_cu(args.cu, S, BL, err_host);
 
   unsigned smask[R], emask[R], wmask[R];
   {
@@ -388,7 +398,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_kernel(const BwdArgs<T, Idx
     carry = compose(carry, tot);
   }
   const bool first_is_head = (head[REV ? R - 1 : 0] >> (REV ? VEC - 1 : 0)) & 1u;
-  const Pfx wpre = tile_prefix<REV>(carry, first_is_head, ticket, args.st, warp, lane);
+  const Pfx wpre = tile_prefix<REV>(carry, first_is_head, ticket, args.st, warp, lane, err_host);
 
 #pragma unroll
   for (int r = 0; r < R; ++r) {
@@ -410,6 +420,7 @@ __global__ void __launch_bounds__(kThreads) scan_bwd_kernel(const BwdArgs<T, Idx
 
 }  // namespace ascan
 
+#include "ascan_slab.cuh"
 #include "ascan_tma.cuh"
 
 namespace ascan {
@@ -460,8 +471,8 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, P, RG>&
                                              const CUtensorMap* const* maps,
                                              const tma::CuView<IdxT>& cu, int64_t N,
                                              int64_t n_tma_total, const tma::TileSched& sch,
-                                             const TileStatus& st, int lane, Extra extra,
-                                             int n_load = NIN) {
+                                             const TileStatus& st, int lane, uint32_t* err_host,
+                                             Extra extra, int n_load = NIN) {
   using namespace tma;
   constexpr int kTileElems = Geo<P>::kTileElems;
   using F = Fmt<T, P>;
@@ -503,7 +514,7 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, P, RG>&
     ++iter;
     if (!mbar_wait_warp(&sm.empty[stage], phase ^ 1u)) {
       if (lane == 0) {
-        report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffeull);
+        report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffeull, err_host);
         set_aborted(st);
       }
       break;
@@ -585,7 +596,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
                                              const CUtensorMap* map_y,
                                              const CUtensorMap* map_gout,
                                              const FwdArgs<T, IdxT>& args, int64_t n_tma_total,
-                                             const tma::TileSched& sch) {
+                                             const tma::TileSched& sch, uint32_t* err_host) {
   using namespace tma;
   constexpr int kPerThread = P, kTileElems = Geo<P>::kTileElems, kBitWords = Geo<P>::kBitWords;
   constexpr uint32_t kThreadMask = Geo<P>::kMask;
@@ -617,7 +628,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
   if (warp == kConsumerWarps) {
     const CUtensorMap* maps[NIN] = {map_g, map_x};
     run_producer<T, IdxT, REV, NIN, NOUT, NS, P, RG>(
-        sm, maps, cu, N, n_tma_total, sch, args.st, lane,
+        sm, maps, cu, N, n_tma_total, sch, args.st, lane, err_host,
         [&](StageMeta<NIN, T, P>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
             uint64_t*) {
           for (uint32_t e = n_tma + ln; e < n_valid; e += 32) {
@@ -628,7 +639,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     return;
   }
 
-  if (blockIdx.x == sch.cta0) validate_cu(args.cu, S, BL);
+  if (blockIdx.x == sch.cta0) validate_cu(args.cu, S, BL, err_host);
   const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
   const ThreadChunks<T, P> tc(o);
   const uint32_t bit_word = o >> 5, bit_shift = o & 31u;
@@ -689,7 +700,8 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     warp_scan<REV>(fold16_inplace<REV>(a, b, head), lane, ex, wtot);
     if (early) take_early(early_raw, te_known, te_meta);
     const Pfx Pc = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
-                                        sch.stride, te_known, te_meta, warp, lane, ok);
+                                        sch.stride, te_known, te_meta, warp, lane, ok,
+                                        err_host);
     // a, b hold the local prefixes: h = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV, P>(head);
     if (IO && lastmask != 0u) record_row_agg<REV>(a, b, lastmask, cm, Pc, p0 + o, BL, args.io.agg);
@@ -750,7 +762,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
   }
   if (!ok && lane == 0) {
     *reinterpret_cast<volatile int*>(&sm.abort) = 1;
-    report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull);
+    report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull, err_host);
     set_aborted(args.st);
   }
   if (lane == 0) bulk_wait_all();
@@ -763,7 +775,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
                                              const CUtensorMap* map_h, const CUtensorMap* map_dx,
                                              const CUtensorMap* map_dg,
                                              const BwdArgs<T, IdxT>& args, int64_t n_tma_total,
-                                             const tma::TileSched& sch) {
+                                             const tma::TileSched& sch, uint32_t* err_host) {
   using namespace tma;
   constexpr int kPerThread = P, kTileElems = Geo<P>::kTileElems, kBitWords = Geo<P>::kBitWords;
   constexpr uint32_t kThreadMask = Geo<P>::kMask;
@@ -796,7 +808,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
   if (warp == kConsumerWarps) {
     const CUtensorMap* maps[NIN] = {map_dy, map_g, map_h};
     run_producer<T, IdxT, REV, NIN, NOUT, NS, P, RG>(
-        sm, maps, cu, N, n_tma_total, sch, args.st, lane,
+        sm, maps, cu, N, n_tma_total, sch, args.st, lane, err_host,
         [&](StageMeta<NIN, T, P>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
             uint64_t* bar) {
           for (uint32_t e = n_tma + ln; e < n_valid; e += 32) {
@@ -848,7 +860,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     return;
   }
 
-  if (blockIdx.x == sch.cta0) validate_cu(args.cu, S, BL);
+  if (blockIdx.x == sch.cta0) validate_cu(args.cu, S, BL, err_host);
   const uint32_t o = static_cast<uint32_t>(tid) * kPerThread;
   const ThreadChunks<T, P> tc(o);
   const uint32_t bit_word = o >> 5, bit_shift = o & 31u;
@@ -957,7 +969,8 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     warp_scan<REV>(fold16_inplace<REV>(gv, dyv, head), lane, ex, wtot);
     if (early) take_early(early_raw, te_known, te_meta);
     const Pfx Pc = warp_tile_prefix<REV>(sm, xi, ex, wtot, first_is_head, ticket, args.st,
-                                        sch.stride, te_known, te_meta, warp, lane, ok);
+                                        sch.stride, te_known, te_meta, warp, lane, ok,
+                                        err_host);
     // gv, dyv hold the local prefixes: dh = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV, P>(head);
     if (IO && lastmask != 0u) record_row_agg<REV>(gv, dyv, lastmask, cm, Pc, p0 + o, BL, args.io.agg);
@@ -1009,7 +1022,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
   }
   if (!ok && lane == 0) {
     *reinterpret_cast<volatile int*>(&sm.abort) = 1;
-    report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull);
+    report(ASCAN_DEV_ERR_LOOKBACK, 0xfffffffdull, err_host);
     set_aborted(args.st);
   }
   if (lane == 0) bulk_wait_all();
@@ -1021,9 +1034,9 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
                         const __grid_constant__ CUtensorMap map_x,
                         const __grid_constant__ CUtensorMap map_y,
                         const __grid_constant__ CUtensorMap map_gout, const FwdArgs<T, IdxT> args,
-                        int64_t n_tma_total, const tma::TileSched sch) {
+                        int64_t n_tma_total, const tma::TileSched sch, uint32_t* err_host) {
   fwd_tma_body<T, IdxT, REV, GATES_OUT, NS, IO, P, RG>(&map_g, &map_x, &map_y, &map_gout, args,
-                                                    n_tma_total, sch);
+                                                    n_tma_total, sch, err_host);
 }
 
 template <typename T, typename IdxT, bool CAUSAL, int NS, bool IO, int P, bool RG>
@@ -1033,9 +1046,9 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
                         const __grid_constant__ CUtensorMap map_h,
                         const __grid_constant__ CUtensorMap map_dx,
                         const __grid_constant__ CUtensorMap map_dg, const BwdArgs<T, IdxT> args,
-                        int64_t n_tma_total, const tma::TileSched sch) {
+                        int64_t n_tma_total, const tma::TileSched sch, uint32_t* err_host) {
   bwd_tma_body<T, IdxT, CAUSAL, NS, IO, P, RG>(&map_dy, &map_g, &map_h, &map_dx, &map_dg, args,
-                                            n_tma_total, sch);
+                                            n_tma_total, sch, err_host);
 }
 
 // Both directions of a bidirectional scan in one launch: CTAs [0, bs.cta0)
@@ -1053,11 +1066,14 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
                              const __grid_constant__ CUtensorMap b_x,
                              const __grid_constant__ CUtensorMap b_y, const FwdArgs<T, IdxT> fa,
                              const FwdArgs<T, IdxT> ba, int64_t n_tma_total,
-                             const tma::TileSched fs, const tma::TileSched bs) {
+                             const tma::TileSched fs, const tma::TileSched bs,
+                             uint32_t* err_host) {
   if (blockIdx.x < bs.cta0)
-    fwd_tma_body<T, IdxT, false, false, NS, false, P, RG>(&f_g, &f_x, &f_y, &f_y, fa, n_tma_total, fs);
+    fwd_tma_body<T, IdxT, false, false, NS, false, P, RG>(&f_g, &f_x, &f_y, &f_y, fa, n_tma_total, fs,
+                                                          err_host);
   else
-    fwd_tma_body<T, IdxT, true, false, NS, false, P, RG>(&b_g, &b_x, &b_y, &b_y, ba, n_tma_total, bs);
+    fwd_tma_body<T, IdxT, true, false, NS, false, P, RG>(&b_g, &b_x, &b_y, &b_y, ba, n_tma_total, bs,
+                                                         err_host);
 }
 
 // Adjoint of scan_fwd_bidi_tma_kernel: the causal adjoint on CTAs [0, bs.cta0),
@@ -1075,12 +1091,14 @@ __global__ void __launch_bounds__(tma::kThreads, tma::kCtasPerSm)
                              const __grid_constant__ CUtensorMap b_dx,
                              const __grid_constant__ CUtensorMap b_dg, const BwdArgs<T, IdxT> fa,
                              const BwdArgs<T, IdxT> ba, int64_t n_tma_total,
-                             const tma::TileSched fs, const tma::TileSched bs) {
+                             const tma::TileSched fs, const tma::TileSched bs,
+                             uint32_t* err_host) {
   if (blockIdx.x < bs.cta0)
-    bwd_tma_body<T, IdxT, true, NS, false, P, RG>(&f_dy, &f_g, &f_h, &f_dx, &f_dg, fa, n_tma_total, fs);
+    bwd_tma_body<T, IdxT, true, NS, false, P, RG>(&f_dy, &f_g, &f_h, &f_dx, &f_dg, fa, n_tma_total, fs,
+                                                  err_host);
   else
     bwd_tma_body<T, IdxT, false, NS, false, P, RG>(&b_dy, &b_g, &b_h, &b_dx, &b_dg, ba, n_tma_total,
-                                                bs);
+                                                bs, err_host);
 }
 
 #if defined(ASCAN_UNIT_MISC)  // compiled in one unit only
@@ -1169,6 +1187,11 @@ __global__ void __launch_bounds__(kThreads)
 // Host side
 // ---------------------------------------------------------------------------
 
+// Device address of the pinned host error flag (ascan_error_flag), or NULL;
+// defined in ascan.cu and passed to every kernel as its last parameter (not
+// inside the argument structs, whose layout the hot kernels are tuned to).
+extern uint32_t* g_err_host;
+
 struct Workspace {
   uint32_t* ticket;
   TileStatus st;
@@ -1223,6 +1246,42 @@ static int launch_status() {
     return ASCAN_ECUDA;
   }
   return ASCAN_OK;
+}
+
+static int sm_count();
+
+// Aggregate-only slab pass by the row reduction of ascan_slab.cuh.  The CTAs
+// of one row combine their parts through the cleared part of the workspace
+// (one counter per row, then one partial per CTA), so a row is split only as
+// far as that room allows.  `r2l`: the fold runs right to left (causal
+// backward, reverse forward).
+template <typename T, typename IdxT, bool BWD>
+static int launch_slab_aggregate(const T* a, const T* b, const IdxT* cu, int64_t S, int64_t C,
+                                 int64_t L, bool r2l, const float* carry, float* agg,
+                                 const Workspace& w, cudaStream_t s) {
+  if (!agg || C <= 0 || L <= 0) return ASCAN_EINVAL;
+  const int64_t sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t target = sms * slab::kAggCtasPerSm;
+  int64_t splits = (target + C - 1) / C;
+  const int64_t by_len = L / 4096 > 1 ? L / 4096 : 1;  // at least a few tiles per warp
+  if (splits > by_len) splits = by_len;
+  char* base = reinterpret_cast<char*>(w.ticket);
+  const size_t counters_bytes = (static_cast<size_t>(C) * 4u + 15u) & ~static_cast<size_t>(15);
+  const size_t room = w.clear_bytes > 256 + counters_bytes ? w.clear_bytes - 256 - counters_bytes : 0;
+  const int64_t by_room = static_cast<int64_t>(room / (8u * static_cast<size_t>(C)));
+  if (splits > by_room) splits = by_room;
+  if (splits < 1) splits = 1;
+  if (C * splits > 0x7fffffffll) return ASCAN_EINVAL;
+  slab::AggArgs<T, IdxT> args{a, b, cu, S, L, C, carry, agg,
+                              reinterpret_cast<uint32_t*>(base + 256),
+                              reinterpret_cast<float2*>(base + 256 + counters_bytes),
+                              static_cast<uint32_t>(splits), g_err_host};
+  const dim3 grid(static_cast<unsigned>(C * splits)), block(slab::kAggThreads);
+  if (r2l)
+    slab::slab_aggregate_kernel<T, IdxT, true, BWD><<<grid, block, 0, s>>>(args);
+  else
+    slab::slab_aggregate_kernel<T, IdxT, false, BWD><<<grid, block, 0, s>>>(args);
+  return launch_status();
 }
 
 // ---- implementation choice ------------------------------------------------
@@ -1496,7 +1555,8 @@ static int launch_fwd_tma_sched(const FwdArgs<T, IdxT>& a, const tma::TileSched&
   FwdArgs<T, IdxT> b = a;
   tma::TileSched sch = sch0;
   b.num_tiles = sch.num_tiles;
-  void* params[] = {&mg, &mx, &my, &mgo, &b, &n_tma_total, &sch};
+  uint32_t* err_host = g_err_host;
+  void* params[] = {&mg, &mx, &my, &mgo, &b, &n_tma_total, &sch, &err_host};
   return launch_cooperative(kern, smem, b.num_tiles, params, s);
 }
 
@@ -1556,7 +1616,8 @@ static int launch_bwd_tma_sched(const BwdArgs<T, IdxT>& a, const tma::TileSched&
   BwdArgs<T, IdxT> b = a;
   tma::TileSched sch = sch0;
   b.num_tiles = sch.num_tiles;
-  void* params[] = {&mdy, &mg, &mh, &mdx, &mdg, &b, &n_tma_total, &sch};
+  uint32_t* err_host = g_err_host;
+  void* params[] = {&mdy, &mg, &mh, &mdx, &mdg, &b, &n_tma_total, &sch, &err_host};
   return launch_cooperative(kern, smem, b.num_tiles, params, s);
 }
 
@@ -1595,14 +1656,14 @@ static void fwd_dispatch(const FwdArgs<T, IdxT>& a, bool reverse, bool gout, cud
   const dim3 grid(a.num_tiles), block(kThreads);
   if (reverse) {
     if (gout)
-      scan_fwd_kernel<T, IdxT, VEC, true, true><<<grid, block, 0, s>>>(a);
+      scan_fwd_kernel<T, IdxT, VEC, true, true><<<grid, block, 0, s>>>(a, g_err_host);
     else
-      scan_fwd_kernel<T, IdxT, VEC, true, false><<<grid, block, 0, s>>>(a);
+      scan_fwd_kernel<T, IdxT, VEC, true, false><<<grid, block, 0, s>>>(a, g_err_host);
   } else {
     if (gout)
-      scan_fwd_kernel<T, IdxT, VEC, false, true><<<grid, block, 0, s>>>(a);
+      scan_fwd_kernel<T, IdxT, VEC, false, true><<<grid, block, 0, s>>>(a, g_err_host);
     else
-      scan_fwd_kernel<T, IdxT, VEC, false, false><<<grid, block, 0, s>>>(a);
+      scan_fwd_kernel<T, IdxT, VEC, false, false><<<grid, block, 0, s>>>(a, g_err_host);
   }
 }
 
@@ -1629,6 +1690,9 @@ int fwd_typed(const void* g, const void* x, void* y, void* gout, const void* cu,
   const bool slab = io.carry || io.halo || io.agg || !y;
   if (slab) {
     if (!vec || a.N < tma::Fmt<T>::kElemsPerRow) return ASCAN_EINVAL;
+    if (!y)  // aggregate-only pass: a row reduction, no scan
+      return launch_slab_aggregate<T, IdxT, false>(a.g, a.x, a.cu, S, C, BL, reverse != 0,
+                                                   io.carry, io.agg, w, s);
     int rc;
     if (reverse)
       rc = gout ? launch_fwd_tma<T, IdxT, true, true>(a, w.allow_ragged, s) : launch_fwd_tma<T, IdxT, true, false>(a, w.allow_ragged, s);
@@ -1655,9 +1719,9 @@ template <typename T, typename IdxT, int VEC>
 static void bwd_dispatch(const BwdArgs<T, IdxT>& a, bool causal, cudaStream_t s) {
   const dim3 grid(a.num_tiles), block(kThreads);
   if (causal)
-    scan_bwd_kernel<T, IdxT, VEC, true><<<grid, block, 0, s>>>(a);
+    scan_bwd_kernel<T, IdxT, VEC, true><<<grid, block, 0, s>>>(a, g_err_host);
   else
-    scan_bwd_kernel<T, IdxT, VEC, false><<<grid, block, 0, s>>>(a);
+    scan_bwd_kernel<T, IdxT, VEC, false><<<grid, block, 0, s>>>(a, g_err_host);
 }
 
 template <typename T, typename IdxT>
@@ -1685,6 +1749,9 @@ int bwd_typed(const void* dy, const void* g, const void* h, void* dx, void* dg,
   const bool slab = io.carry || io.halo || io.agg || !dx;
   if (slab) {
     if (!vec || a.N < tma::Fmt<T>::kElemsPerRow) return ASCAN_EINVAL;
+    if (!dx)  // aggregate-only pass: a row reduction, no scan (the states are not read)
+      return launch_slab_aggregate<T, IdxT, true>(a.g, a.dy, a.cu, S, C, BL, causal != 0,
+                                                  io.carry, io.agg, w, s);
     const int rc = causal ? launch_bwd_tma<T, IdxT, true>(a, w.allow_ragged, s) : launch_bwd_tma<T, IdxT, false>(a, w.allow_ragged, s);
     return rc > 0 ? ASCAN_OK : (rc == 0 ? ASCAN_EINVAL : rc);
   }
@@ -1727,7 +1794,8 @@ static int launch_fwd_bidi_sched(const FwdArgs<T, IdxT>& fa, const FwdArgs<T, Id
   FwdArgs<T, IdxT> f = fa, b = ba;
   f.num_tiles = fs.num_tiles;
   b.num_tiles = bs.num_tiles;
-  void* params[] = {&fg, &fx, &fy, &bg, &bx, &by, &f, &b, &n_tma_total, &fs, &bs};
+  uint32_t* err_host = g_err_host;
+  void* params[] = {&fg, &fx, &fy, &bg, &bx, &by, &f, &b, &n_tma_total, &fs, &bs, &err_host};
   return launch_coop_grid(kern, smem, grid, params, s);
 }
 
@@ -1759,8 +1827,9 @@ static int launch_bwd_bidi_sched(const BwdArgs<T, IdxT>& fa, const BwdArgs<T, Id
   BwdArgs<T, IdxT> f = fa, b = ba;
   f.num_tiles = fs.num_tiles;
   b.num_tiles = bs.num_tiles;
+  uint32_t* err_host = g_err_host;
   void* params[] = {&m[0], &m[1], &m[2], &m[3], &m[4], &m[5], &m[6], &m[7], &m[8], &m[9],
-                    &f,    &b,    &n_tma_total, &fs, &bs};
+                    &f,    &b,    &n_tma_total, &fs, &bs, &err_host};
   return launch_coop_grid(kern, smem, grid, params, s);
 }
 

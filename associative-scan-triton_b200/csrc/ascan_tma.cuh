@@ -802,7 +802,7 @@ __device__ __forceinline__ Pfx warp_tile_prefix(Sm& sm, uint32_t xi, Pfx thread_
                                                 Pfx warp_total, bool first_is_head,
                                                 uint32_t ticket, const TileStatus& st,
                                                 uint32_t stride, bool te_known, Pfx te_known_val,
-                                                int warp, int lane, bool& ok) {
+                                                int warp, int lane, bool& ok, uint32_t* err_host) {
   constexpr int kLast = kConsumerWarps - 1;
   const int lw = REV ? kLast - warp : warp;  // position of this warp in scan order
   const bool need_lookback = !first_is_head && ticket >= stride;  // else a row's first tile
@@ -813,7 +813,7 @@ __device__ __forceinline__ Pfx warp_tile_prefix(Sm& sm, uint32_t xi, Pfx thread_
     if (!te_known) {
       bool timed_out = false;
       te = lookback_warp<kLookbackPerLane>(st, ticket, lane, &timed_out, stride);
-      if (timed_out && lane == 0) report(ASCAN_DEV_ERR_LOOKBACK, ticket);
+      if (timed_out && lane == 0) report(ASCAN_DEV_ERR_LOOKBACK, ticket, err_host);
     }
     if (lane == 0) xs_put(&slot.te, te, ticket);
   }

@@ -25,8 +25,9 @@
  *     argument or a CUDA launch failure.  Problems only visible on the device
  *     (a cu_seqlens that is not monotone or does not end at seq_total, a tile
  *     whose predecessor never published) set a sticky per-device error word
- *     read by ascan_get_device_error().  No device-side condition can make a
- *     kernel trap, hang or touch memory outside the arrays it was given.
+ *     read by ascan_get_device_error(), and the host-visible flag of
+ *     ascan_error_flag() once it is enabled.  No device-side condition can
+ *     make a kernel trap, hang or touch memory outside the arrays it was given.
  */
 #ifndef ASCAN_H_
 #define ASCAN_H_
@@ -172,7 +173,8 @@ ASCAN_API int ascan_forward_noalloc(const void* gates, const void* tokens, void*
  *   row_aggregate [C][2] output: the inclusive (gate product, state) at each
  *                 row's last element in scan order (NULL: not written).
  *   tokens_out may be NULL together with gates_out for an aggregate-only pass
- *   (reads gates and tokens, writes only row_aggregate).
+ *   (reads gates and tokens, writes only row_aggregate): a row reduction over
+ *   the row's last sequence piece in scan order, no scan.
  * ascan_backward_slab: ascan_backward plus
  *   row_carry      [C] additive term for the adjoint at each row's first
  *                  element in scan order (causal: the slab's last column):
@@ -186,7 +188,9 @@ ASCAN_API int ascan_forward_noalloc(const void* gates, const void* tokens, void*
  *                  each row's last element in scan order, where the product
  *                  leaves out the first element's coefficient (it lives in
  *                  row_carry).
- *   d_tokens and d_gates may both be NULL for an aggregate-only pass.
+ *   d_tokens and d_gates may both be NULL for an aggregate-only pass (a row
+ *   reduction over the row's first sequence piece in array order for the
+ *   causal adjoint; the states are not read).
  */
 ASCAN_API int ascan_forward_slab(const void* gates, const void* tokens, void* tokens_out,
                                  void* gates_out, const void* cu_seqlens, int cu_index_type,
@@ -200,6 +204,31 @@ ASCAN_API int ascan_backward_slab(const void* grad, const void* gates, const voi
                                   int64_t seq_total, int dtype, int causal, const float* row_carry,
                                   const float* row_state_halo, float* row_aggregate,
                                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Carry fold of a time-sharded run (no counterpart in the reference): the
+ * carry that enters slab `rank` of `world` (world <= 32), from the records all
+ * ranks contributed to one all-gather -- record j (record_floats floats,
+ * device memory) is rank j's:
+ *   direction 0 (forward):  [0, 2C)  ascan_forward_slab's row_aggregate of
+ *                                    slab j (gate product, state) per row
+ *      -> carry_out [C][2]: row_carry for ascan_forward_slab; halo_out NULL
+ *   direction 1 (backward): [0, 2C)  ascan_backward_slab's row_aggregate of
+ *                                    slab j (from a zero row_carry)
+ *                           [2C, 3C) slab j's first gate column g[t0_j]
+ *                           [3C, 4C) slab j's last state column h[t1_j - 1]
+ *      -> carry_out [C]: row_carry for ascan_backward_slab; halo_out [C]
+ *         (nullable): row_state_halo, h[t0 - 1] or 0 at a sequence start
+ * starts_new_mask bit j: a sequence starts at slab j's first column;
+ * inner_boundary_mask bit j: a sequence boundary lies strictly inside slab j.
+ * One small kernel on `stream`; replaces a host loop over the ranks
+ * (associative_scan_triton/time_shard.py: forward_carry, backward_carry,
+ * state_halo restate it).
+ */
+ASCAN_API int ascan_time_shard_fold(const float* records, int64_t record_floats, int world,
+                                    int rank, int64_t num_channels, uint32_t starts_new_mask,
+                                    uint32_t inner_boundary_mask, int direction,
+                                    float* carry_out, float* halo_out, void* stream);
 
 /*
  * Bidirectional pair in one launch: the causal scan of (gates_fwd,
@@ -308,7 +337,21 @@ ASCAN_API int ascan_get_device_error(int device, unsigned int* code, long long* 
 ASCAN_API int ascan_selftest_waits(void* workspace, size_t workspace_bytes, long long limit_ns,
                                    long long* results, void* stream);
 
-/* Reset the sticky error word of `device`. */
+/*
+ * Host-visible error flag (no counterpart in the reference): the address of a
+ * word of pinned, mapped host memory that every kernel which sets a bit of
+ * the sticky device error word also writes (with that error's bits), so a
+ * caller can poll for device-side errors after each call without
+ * synchronising.  The first call allocates the word (cudaHostAlloc, mapped
+ * and portable; make it before any stream capture) and enables it for every
+ * launch that follows, in every thread and on every device of the process.
+ * Concurrent reports may overwrite each other's bits in this word; the sticky
+ * word (ascan_get_device_error) keeps all of them.  ascan_clear_device_error
+ * zeroes it.  Returns NULL when it cannot be allocated (no device).
+ */
+ASCAN_API volatile unsigned int* ascan_error_flag(void);
+
+/* Reset the sticky error word of `device` (and the host-visible flag). */
 ASCAN_API int ascan_clear_device_error(int device);
 
 #ifdef __cplusplus

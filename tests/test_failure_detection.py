@@ -6,7 +6,9 @@ predecessor turns into an error status instead of a hang.  Here the waits
 are run on conditions that nothing ever satisfies (a flag nobody sets), with
 a short limit, through ``ascan_selftest_waits``; then an ordinary scan checks
 that the context is still usable.  Malformed ``cu_seqlens`` -- the failure a
-caller can actually plant -- are covered in ``test_scan_kernels.py``.
+caller can actually plant -- are covered in ``test_scan_kernels.py`` with
+sync checking on, and here with it off: the host-visible error flag makes a
+later op raise without any synchronisation in the ops themselves.
 """
 
 from __future__ import annotations
@@ -52,3 +54,35 @@ def test_unsatisfied_waits_give_up_and_the_context_survives(limit_ms):
   torch.cuda.synchronize()
   gold, _ = oracle.scan_fwd(g, x, cu)
   assert_close_to_gold(y, gold, torch.float32, "scan after the self-test")
+
+
+@pytest.mark.gpu
+def test_device_error_surfaces_without_sync_checking():
+  """A cu_seqlens that does not end at BL, passed with sync checking off: the
+  call itself returns (the kernel runs asynchronously, stays in bounds and
+  reports), and once it has run the following op raises ScanError from the
+  host-visible flag.  The reference reads out of bounds silently here
+  (reference tests/test_scan_kernels.py:45-83)."""
+  g, x = make_inputs(3, 1000, gate="long")
+  y = torch.empty_like(x)
+  bad = cu_of([400, 700])  # ends at 1100 > BL = 1000
+  good = cu_of([400, 600])
+  was = _lib.sync_check_enabled()
+  _lib.set_sync_check(False)
+  try:
+    _lib.clear_device_error()
+    assert _lib.error_flag() == 0
+    _lib.forward(g, x, y, None, bad, 2, 3, False)  # no exception: nothing synchronised
+    torch.cuda.synchronize()                       # the failing kernel has run
+    assert _lib.error_flag() & _lib.DEV_ERR_CU_END
+    with pytest.raises(_lib.ScanError, match="cu_seqlens"):
+      _lib.forward(g, x, y, None, good, 2, 3, False)
+    # reading the error cleared it: the next ops run and are right
+    assert _lib.error_flag() == 0
+    _lib.forward(g, x, y, None, good, 2, 3, False)
+    torch.cuda.synchronize()
+    assert _lib.error_flag() == 0
+  finally:
+    _lib.set_sync_check(was)
+  gold, _ = oracle.scan_fwd(g, x, good)
+  assert_close_to_gold(y, gold, torch.float32, "scan after the reported error")

@@ -217,6 +217,155 @@ def test_slab_aggregate_matches_definition():
   np.testing.assert_allclose(bagg.cpu().numpy(), bwant, rtol=1e-5, atol=1e-6)
 
 
+def _slab_agg_reference(g, v, cu, forward, r2l, carry):
+  """fp64 restatement of a slab pass's row aggregate: the scan of the whole
+  row in scan order (heads restart the value and the coefficient product with
+  the head's own coefficient; the row carry enters at the row's first element
+  in scan order), read at the row's last element in scan order.  Backward:
+  coefficient g[t+1] (causal) or g[t-1] (reverse), 1 for the row's first
+  element in scan order."""
+  C, L = g.shape
+  cu = [int(c) for c in cu]
+  starts = {c for c in cu[:-1] if c < L}
+  ends = {c - 1 for c in cu[1:] if c > 0}
+  order = list(range(L - 1, -1, -1)) if r2l else list(range(L))
+  heads = ends if r2l else starts
+  coeff = np.ones((C, L))
+  if forward:
+    coeff[:] = g
+  elif r2l:
+    coeff[:, :-1] = g[:, 1:]
+  else:
+    coeff[:, 1:] = g[:, :-1]
+  A, Y = np.ones(C), np.zeros(C)
+  for k, t in enumerate(order):
+    a, b = coeff[:, t].copy(), v[:, t].copy()
+    if k == 0 and carry is not None:
+      if forward:
+        b, a = b + a * carry[:, 1], a * carry[:, 0]
+      else:
+        b, a = b + carry, np.ones(C)
+    if k == 0 or t in heads:
+      A, Y = a, b
+    else:
+      Y, A = a * Y + b, A * a
+  return np.stack([A, Y], axis=1)
+
+
+SLAB_AGG_CASES = [
+  (6, 8320, [0, 8320]),                      # one sequence, two CTAs per row
+  (6, 8320, [0, 3000, 8320]),                # an inner boundary
+  (6, 8320, [0, 1, 8319, 8320]),             # one-element pieces at both ends
+  (3, 300_000, [0, 300_000]),                # many CTAs per row
+  (3, 300_000, [0, 77, 299_000, 300_000]),
+  (1500, 1024, [0, 1024]),                   # many short rows, one CTA each
+  (5, 4101, [0, 4101]),                      # rows not a whole number of vectors
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(("C", "L", "cu"), SLAB_AGG_CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("with_carry", [False, True])
+def test_slab_aggregate_reduction_matches_definition(C, L, cu, dtype, with_carry):
+  from associative_scan_triton import _lib
+  g, x = make_inputs(C, L, dtype=dtype, gate="verylong", seed=C + L)
+  dy = torch.randn(C, L, generator=torch.Generator().manual_seed(L)).to("cuda", dtype)
+  h = torch.randn(C, L, device="cuda").to(dtype)
+  cu_t = torch.tensor(cu, dtype=torch.int64, device="cuda")
+  gd, xd, dyd = (t.double().cpu().numpy() for t in (g, x, dy))
+  rng = np.random.default_rng(1)
+  carry_f = np.stack([rng.uniform(0.5, 1.0, C), rng.standard_normal(C)], 1)
+  carry_b = rng.standard_normal(C)
+  for reverse in (False, True):
+    agg = torch.empty(C, 2, device="cuda")
+    carry = torch.tensor(carry_f, dtype=torch.float32, device="cuda") if with_carry else None
+    _lib.forward_slab(g, x, None, None, cu_t, len(cu) - 1, C, reverse, row_carry=carry,
+                      row_aggregate=agg)
+    want = _slab_agg_reference(gd, xd, cu, True, reverse,
+                               carry.double().cpu().numpy() if with_carry else None)
+    np.testing.assert_allclose(agg.cpu().numpy(), want, rtol=1e-4, atol=1e-5,
+                               err_msg=f"forward aggregate reverse={reverse}")
+  for causal in (True, False):
+    agg = torch.empty(C, 2, device="cuda")
+    carry = torch.tensor(carry_b, dtype=torch.float32, device="cuda") if with_carry else None
+    _lib.backward_slab(dy, g, h, None, None, cu_t, len(cu) - 1, C, causal, row_carry=carry,
+                       row_aggregate=agg)
+    want = _slab_agg_reference(gd, dyd, cu, False, causal,
+                               carry.double().cpu().numpy() if with_carry else None)
+    np.testing.assert_allclose(agg.cpu().numpy(), want, rtol=1e-4, atol=1e-5,
+                               err_msg=f"backward aggregate causal={causal}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(("world", "cu"), [
+  (2, [0, 512]), (4, [0, 512]), (4, [0, 100, 128, 300, 512]), (8, [0, 64, 65, 448, 512]),
+])
+def test_device_fold_matches_host_fold(world, cu):
+  """ascan_time_shard_fold against forward_carry / backward_carry /
+  state_halo on the same random records, for every rank."""
+  C = 37
+  bounds = ts.even_bounds(512, world, align=8)
+  plans = ts.plan_slabs(cu, bounds)
+  gen = torch.Generator().manual_seed(world)
+  fwd = [torch.stack([0.5 + 0.5 * torch.rand(C, generator=gen), torch.randn(C, generator=gen)], 1)
+         for _ in range(world)]
+  bwd = [torch.stack([0.5 + 0.5 * torch.rand(C, generator=gen), torch.randn(C, generator=gen)], 1)
+         for _ in range(world)]
+  firsts = [torch.rand(C, generator=gen) for _ in range(world)]
+  lasts = [torch.randn(C, generator=gen) for _ in range(world)]
+  rec_f = torch.stack([a.reshape(-1) for a in fwd]).cuda()
+  rec_b = torch.stack([torch.cat([a.reshape(-1), f, l]) for a, f, l in zip(bwd, firsts, lasts)]).cuda()
+  for rank in range(world):
+    dev = ts.fold_forward(rec_f, plans, rank)
+    host = ts.forward_carry(plans, fwd, rank)
+    torch.testing.assert_close(dev.cpu(), host, rtol=1e-6, atol=1e-6)
+    carry, halo = ts.fold_backward(rec_b, plans, rank)
+    torch.testing.assert_close(carry.cpu(), ts.backward_carry(plans, bwd, firsts, rank),
+                               rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(halo.cpu(), ts.state_halo(plans, lasts, rank), rtol=0, atol=0)
+
+
+@pytest.mark.gpu
+def test_time_shard_step_with_list_exchange_matches_oracle():
+  """TimeShardStep (the multi-rank driver's step object) on every slab of one
+  GPU, its all-gather replaced by writes into the shared buffer: forward and
+  backward slabs against the fp64 oracle on the whole axis."""
+  C, T, world = 8, 1 << 16, 4
+  cu = [0, 10000, 1 << 14, 40000, T]
+  g, x = make_inputs(C, T, gate="verylong", seed=9)
+  dy = torch.randn(C, T, generator=torch.Generator().manual_seed(2)).cuda()
+  bounds = ts.even_bounds(T, world, align=64)
+  plans = ts.plan_slabs(cu, bounds)
+  sl = [slice(a, b) for a, b in zip(bounds, bounds[1:])]
+  shared = {}
+
+  def gather_for(k):
+    def gather(out, inp):  # every rank's record lands in one buffer per direction
+      buf = shared.setdefault(out.shape, torch.zeros_like(out))
+      buf[k].copy_(inp)
+      out.copy_(buf)
+    return gather
+
+  steps = [ts.TimeShardStep((C, b - a), g.dtype, plans, k, "cuda", gather=gather_for(k))
+           for k, (a, b) in enumerate(zip(bounds, bounds[1:]))]
+  gs = [g[:, s].contiguous() for s in sl]
+  xs = [x[:, s].contiguous() for s in sl]
+  dys = [dy[:, s].contiguous() for s in sl]
+  # two sweeps over the ranks: the first fills every record, the second reads them all
+  for _ in range(2):
+    ys = [st.forward(gk, xk) for st, gk, xk in zip(steps, gs, xs)]
+  y = torch.cat(ys, 1)
+  cu_t = torch.tensor(cu, dtype=torch.int64)
+  gold_y, _ = oracle.scan_fwd(g, x, cu_t)
+  assert_close_to_gold(y, gold_y, torch.float32, "TimeShardStep y")
+  for _ in range(2):
+    grads = [st.backward(dk, gk, yk) for st, dk, gk, yk in zip(steps, dys, gs, ys)]
+  gdx, gdg = oracle.scan_bwd(dy, g, y, cu_t)
+  assert_close_to_gold(torch.cat([d[1] for d in grads], 1), gdx, torch.float32, "TimeShardStep dx")
+  assert_close_to_gold(torch.cat([d[0] for d in grads], 1), gdg, torch.float32, "TimeShardStep dg")
+
+
 @pytest.mark.gpu
 def test_slab_entry_points_refuse_unaligned_views():
   from associative_scan_triton import _lib
