@@ -1260,11 +1260,9 @@ static int launch_slab_aggregate(const T* a, const T* b, const IdxT* cu, int64_t
                                  int64_t L, bool r2l, const float* carry, float* agg,
                                  const Workspace& w, cudaStream_t s) {
   if (!agg || C <= 0 || L <= 0) return ASCAN_EINVAL;
-  const int64_t sms = sm_count() > 0 ? sm_count() : 148;
-  const int64_t target = sms * slab::kAggCtasPerSm;
-  int64_t splits = (target + C - 1) / C;
-  const int64_t by_len = L / 4096 > 1 ? L / 4096 : 1;  // at least a few tiles per warp
-  if (splits > by_len) splits = by_len;
+  // every row in parts of about kAggPart elements, so that the grid is many
+  // short waves of CTAs (a small tail) whatever the number of rows
+  int64_t splits = (L + slab::kAggPart / 2) / slab::kAggPart;
   char* base = reinterpret_cast<char*>(w.ticket);
   const size_t counters_bytes = (static_cast<size_t>(C) * 4u + 15u) & ~static_cast<size_t>(15);
   const size_t room = w.clear_bytes > 256 + counters_bytes ? w.clear_bytes - 256 - counters_bytes : 0;

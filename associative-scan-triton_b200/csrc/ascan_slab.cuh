@@ -35,8 +35,9 @@ namespace slab {
 
 constexpr int kAggThreads = 256;
 constexpr int kAggWarps = kAggThreads / 32;
-constexpr int kAggUnroll = 4;     // 32-vector tiles per warp in flight
-constexpr int kAggCtasPerSm = 8;  // target residency for the grid size
+constexpr int kAggUnroll = 4;       // 32-vector tiles per warp in flight
+constexpr int kAggCtasPerSm = 4;    // 64 registers per thread: no spills
+constexpr int64_t kAggPart = 16384; // elements of a row per CTA (many short waves, small tail)
 
 template <typename T, typename IdxT>
 struct AggArgs {

@@ -116,3 +116,34 @@ def test_compiled_causal_vs_oracle():
   assert_close_to_gold(y, gy, torch.float32, "y")
   assert_close_to_gold(x.grad, gdx, torch.float32, "dx")
   assert_close_to_gold(g.grad, gdg, torch.float32, "dg")
+
+
+def test_reference_named_ops_keep_the_reference_schema():
+  """torch.ops.associative_scan_triton.scan_causal_fwd / scan_bidi_fwd return
+  what the reference's triton_ops return (reference
+  src/associative_scan_triton/scan_compiled.py:89-113, :208-240): the states
+  plus a copy of the gates, and gradients flow to gates and tokens."""
+  C, cu = 16, _cu(2, 300)
+  total = int(cu[-1])
+  grid = ast.get_grid(len(cu), 300, 128, C)
+  g = torch.rand(C, total, device=DEV, requires_grad=True)
+  x = torch.randn(C, total, device=DEV, requires_grad=True)
+  y, g_copy = torch.ops.associative_scan_triton.scan_causal_fwd(g, x, cu, grid[1], C, 128)
+  assert torch.equal(g_copy, g.detach()) and g_copy.data_ptr() != g.data_ptr()
+  gold, _ = oracle.scan_fwd(g, x, cu)
+  assert_close_to_gold(y, gold, torch.float32, "scan_causal_fwd states")
+  y.sum().backward()
+  want_dg, want_dx = g.grad.clone(), x.grad.clone()
+  g.grad = x.grad = None
+  args = {"cu_seqlens": cu, "chunk_size": 128, "grid": grid}
+  ast.scan_causal_compiled(g, x, args).sum().backward()
+  torch.testing.assert_close(g.grad, want_dg, rtol=0, atol=0)
+  torch.testing.assert_close(x.grad, want_dx, rtol=0, atol=0)
+  t = [torch.rand(C, total, device=DEV), torch.randn(C, total, device=DEV),
+       torch.rand(C, total, device=DEV), torch.randn(C, total, device=DEV)]
+  outs = torch.ops.associative_scan_triton.scan_bidi_fwd(*t, cu, grid[1], C, 128)
+  assert len(outs) == 4
+  assert torch.equal(outs[2], t[0]) and torch.equal(outs[3], t[2])
+  ref_fwd, ref_bwd = ast.scan_bidirectional_branched_compiled(*t, args)
+  torch.testing.assert_close(outs[0], ref_fwd, rtol=0, atol=0)
+  torch.testing.assert_close(outs[1], ref_bwd, rtol=0, atol=0)

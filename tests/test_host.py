@@ -181,8 +181,13 @@ def test_public_api_surface():
 def test_custom_ops_registered():
   ops = torch.ops.associative_scan_triton
   for name in ("scan_causal_fwd", "scan_causal_bwd", "scan_bidi_fwd", "scan_bidi_bwd",
-               "shift_pad"):
+               "shift_pad", "scan_causal_fwd_noclone", "scan_bidi_fwd_noclone"):
     assert hasattr(ops, name), name
+  # the reference-named forward ops keep the reference's outputs: states + gates copies
+  # (reference src/associative_scan_triton/scan_compiled.py:89-97, :208-218)
+  assert len(ops.scan_causal_fwd.default._schema.returns) == 2
+  assert len(ops.scan_bidi_fwd.default._schema.returns) == 4
+  assert len(ops.scan_causal_fwd_noclone.default._schema.returns) == 1
 
 
 def test_custom_ops_have_fake_kernels():
@@ -192,7 +197,9 @@ def test_custom_ops_have_fake_kernels():
     g = torch.empty(3, 16, device="cuda")
     x = torch.empty(3, 16, device="cuda")
     cu = torch.empty(2, dtype=torch.int32, device="cuda")
-    y = torch.ops.associative_scan_triton.scan_causal_fwd(g, x, cu, 1, 3, 16)
+    y, g_copy = torch.ops.associative_scan_triton.scan_causal_fwd(g, x, cu, 1, 3, 16)
+    assert y.shape == g_copy.shape == (3, 16)
+    y = torch.ops.associative_scan_triton.scan_causal_fwd_noclone(g, x, cu, 1, 3, 16)
     assert y.shape == (3, 16)
     dg, dx = torch.ops.associative_scan_triton.scan_causal_bwd(y, g, y, cu, 1, 3, 16)
     assert dg.shape == dx.shape == (3, 16)
