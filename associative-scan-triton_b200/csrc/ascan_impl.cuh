@@ -530,9 +530,13 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, P, RG>&
     }
     int64_t p0, t0, limit;
     if (sch.row_mode) {
-      const uint32_t j = ticket / sch.rows;
-      const uint32_t c = ticket - j * sch.rows;
-      const uint32_t jj = REV ? sch.tiles_per_row - 1u - j : j;
+      // stride = rows * segs: the (row, segment) pairs of one tile column
+      const uint32_t j = ticket / sch.stride;
+      const uint32_t v = ticket - j * sch.stride;
+      const uint32_t c = v / sch.segs;
+      const uint32_t seg = v - c * sch.segs;
+      const uint32_t per_seg = sch.tiles_per_row / sch.segs;
+      const uint32_t jj = seg * per_seg + (REV ? per_seg - 1u - j : j);
       t0 = static_cast<int64_t>(jj) * kTileElems;
       p0 = static_cast<int64_t>(c) * BL + t0;
       limit = static_cast<int64_t>(c) * BL + BL;
@@ -596,7 +600,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
                                              const CUtensorMap* map_y,
                                              const CUtensorMap* map_gout,
                                              const FwdArgs<T, IdxT>& args, int64_t n_tma_total,
-                                             const tma::TileSched& sch, uint32_t* err_host) {
+                                             const tma::TileSched& sch_in, uint32_t* err_host) {
   using namespace tma;
   constexpr int kPerThread = P, kTileElems = Geo<P>::kTileElems, kBitWords = Geo<P>::kBitWords;
   constexpr uint32_t kThreadMask = Geo<P>::kMask;
@@ -608,8 +612,17 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
   const int64_t S = args.S, BL = args.BL, N = args.N;
 
   const bool cache_cu = (S + 1) <= kCuCache;
+  // segment mode needs cu_seqlens[i] == i * BL / segs: each thread checks the
+  // entries it caches, the start-up barrier takes the vote (time-slab
+  // launches never take it)
+  bool seg_ok = !IO && sch_in.segs > 1u && cache_cu;
+  const int64_t seg_len = seg_ok ? BL / sch_in.segs : 0;
   if (cache_cu)
-    for (int64_t i = tid; i <= S; i += tma::kThreads) sm.cu[i] = cu_at(args.cu, i, BL);
+    for (int64_t i = tid; i <= S; i += tma::kThreads) {
+      const int64_t v = cu_at(args.cu, i, BL);
+      sm.cu[i] = v;
+      seg_ok = seg_ok && v == i * seg_len;
+    }
   if (tid < kXsRing * (kConsumerWarps + 1)) {
     float4* f = &sm.xs[0].warp[0] + tid;
     f->w = __uint_as_float(kNoTag);
@@ -622,7 +635,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  __syncthreads();
+  const tma::TileSched sch = tma::seg_sched(sch_in, __syncthreads_and(seg_ok) != 0);
   const CuView<IdxT> cu{args.cu, cache_cu ? sm.cu : nullptr, S, BL};
 
   if (warp == kConsumerWarps) {
@@ -775,21 +788,31 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
                                              const CUtensorMap* map_h, const CUtensorMap* map_dx,
                                              const CUtensorMap* map_dg,
                                              const BwdArgs<T, IdxT>& args, int64_t n_tma_total,
-                                             const tma::TileSched& sch, uint32_t* err_host) {
+                                             const tma::TileSched& sch_in, uint32_t* err_host) {
   using namespace tma;
   constexpr int kPerThread = P, kTileElems = Geo<P>::kTileElems, kBitWords = Geo<P>::kBitWords;
   constexpr uint32_t kThreadMask = Geo<P>::kMask;
   using F = Fmt<T, P>;
   constexpr bool REV = CAUSAL;
   constexpr int NIN = 3, NOUT = 2;
+  constexpr bool kPackH = sizeof(T) == 2 && !RG && !IO;
   using Sm = Smem<NIN, NOUT, NS, T, P, RG>;
   Sm& sm = smem_view<Sm>();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t S = args.S, BL = args.BL, N = args.N;
 
   const bool cache_cu = (S + 1) <= kCuCache;
+  // segment mode needs cu_seqlens[i] == i * BL / segs: each thread checks the
+  // entries it caches, the start-up barrier takes the vote (time-slab
+  // launches never take it)
+  bool seg_ok = !IO && sch_in.segs > 1u && cache_cu;
+  const int64_t seg_len = seg_ok ? BL / sch_in.segs : 0;
   if (cache_cu)
-    for (int64_t i = tid; i <= S; i += tma::kThreads) sm.cu[i] = cu_at(args.cu, i, BL);
+    for (int64_t i = tid; i <= S; i += tma::kThreads) {
+      const int64_t v = cu_at(args.cu, i, BL);
+      sm.cu[i] = v;
+      seg_ok = seg_ok && v == i * seg_len;
+    }
   if (tid < kXsRing * (kConsumerWarps + 1)) {
     float4* f = &sm.xs[0].warp[0] + tid;
     f->w = __uint_as_float(kNoTag);
@@ -802,7 +825,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  __syncthreads();
+  const tma::TileSched sch = tma::seg_sched(sch_in, __syncthreads_and(seg_ok) != 0);
   const CuView<IdxT> cu{args.cu, cache_cu ? sm.cu : nullptr, S, BL};
 
   if (warp == kConsumerWarps) {
@@ -883,7 +906,11 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     const int64_t p0 = m.p0;
     const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
     const bool has_outside = m.has_outside != 0u;
-    float dyv[kPerThread], gv[kPerThread], hv[kPerThread];
+    float dyv[kPerThread], gv[kPerThread];
+    // 16-bit states stay packed (two per word) until the dg epilogue: half the
+    // registers of floats through the scan and the carry
+    float hv[kPackH ? 1 : kPerThread];
+    uint32_t hw[kPackH ? kPerThread / 2 : 1];
     // ragged rows: the tile sits `shift` elements into its buffers
     const uint32_t shift = RG ? m.shift : 0u;
     if constexpr (RG) {
@@ -893,7 +920,10 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     } else {
       read_block<T, NIN>(sm.in[stage][0], tc, m, 0, o, n_tma, n_valid, 0.f, dyv);
       read_block<T, NIN>(sm.in[stage][1], tc, m, 1, o, n_tma, n_valid, 1.f, gv);
-      read_block<T, NIN>(sm.in[stage][2], tc, m, 2, o, n_tma, n_valid, 0.f, hv);
+      if constexpr (kPackH)
+        read_block_packed<T, NIN>(sm.in[stage][2], tc, m, 2, o, n_tma, n_valid, hw);
+      else
+        read_block<T, NIN>(sm.in[stage][2], tc, m, 2, o, n_tma, n_valid, 0.f, hv);
     }
     // neighbours across the thread boundary: from the tile, or the tile-edge halo
     constexpr int V = 16 / static_cast<int>(sizeof(T));
@@ -940,21 +970,26 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
       phase ^= 1u;
     }
 
-    // a[t] = g[t+1], hn[t] = h[t-1] (causal) or the mirror image
+    // a[t] = g[t+1], hn[t] = h[t-1] (causal) or the mirror image (packed
+    // states are shifted when they are unpacked)
     if (CAUSAL) {
 #pragma unroll
       for (int j = 0; j < kPerThread - 1; ++j) gv[j] = gv[j + 1];
       gv[kPerThread - 1] = g_nb;
+      if constexpr (!kPackH) {
 #pragma unroll
-      for (int j = kPerThread - 1; j > 0; --j) hv[j] = hv[j - 1];
-      hv[0] = h_nb;
+        for (int j = kPerThread - 1; j > 0; --j) hv[j] = hv[j - 1];
+        hv[0] = h_nb;
+      }
     } else {
 #pragma unroll
       for (int j = kPerThread - 1; j > 0; --j) gv[j] = gv[j - 1];
       gv[0] = g_nb;
+      if constexpr (!kPackH) {
 #pragma unroll
-      for (int j = 0; j < kPerThread - 1; ++j) hv[j] = hv[j + 1];
-      hv[kPerThread - 1] = h_nb;
+        for (int j = 0; j < kPerThread - 1; ++j) hv[j] = hv[j + 1];
+        hv[kPerThread - 1] = h_nb;
+      }
     }
     const uint32_t head = CAUSAL ? emask : smask;
     uint32_t tail = CAUSAL ? smask : emask;
@@ -963,8 +998,10 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     const uint32_t lastmask = IO && args.io.agg ? tail : 0u;
     if (IO && args.io.carry != nullptr && head != 0u)
       apply_row_carry_adjoint<CAUSAL>(gv, dyv, head, p0 + o, BL, args.io.carry);
-    if (IO && args.io.halo != nullptr && tail != 0u)
-      tail &= ~apply_row_halo<CAUSAL>(hv, tail, p0 + o, BL, args.io.halo);
+    if constexpr (IO) {
+      if (args.io.halo != nullptr && tail != 0u)
+        tail &= ~apply_row_halo<CAUSAL>(hv, tail, p0 + o, BL, args.io.halo);
+    }
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(gv, dyv, head), lane, ex, wtot);
     if (early) take_early(early_raw, te_known, te_meta);
@@ -977,8 +1014,17 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
       const float d = ((cm >> j) & 1u) ? fmaf(gv[j], Pc.b, dyv[j]) : dyv[j];
+      float hn;
+      if constexpr (kPackH) {
+        if (CAUSAL)
+          hn = j == 0 ? h_nb : packed_elem<T>(hw, j - 1);
+        else
+          hn = j == kPerThread - 1 ? h_nb : packed_elem<T>(hw, j + 1);
+      } else {
+        hn = hv[j];
+      }
       dyv[j] = d;                                    // dx
-      gv[j] = ((tail >> j) & 1u) ? 0.f : d * hv[j];  // dg
+      gv[j] = ((tail >> j) & 1u) ? 0.f : d * hn;     // dg
     }
     const bool store = !IO || args.dx != nullptr;  // false: aggregate-only pass
     const uint32_t valid = below_mask<P>(o, n_valid) & ~omask;
@@ -1250,31 +1296,48 @@ static int launch_status() {
 
 static int sm_count();
 
-// Aggregate-only slab pass by the row reduction of ascan_slab.cuh.  The CTAs
-// of one row combine their parts through the cleared part of the workspace
-// (one counter per row, then one partial per CTA), so a row is split only as
-// far as that room allows.  `r2l`: the fold runs right to left (causal
-// backward, reverse forward).
+// Aggregate-only slab pass by the row reduction of ascan_slab.cuh.  The warps
+// that share a row combine their parts through the cleared part of the
+// workspace (one counter per row, then one partial per warp and row), so the
+// grid is only as wide as that room allows.  `r2l`: the fold runs right to
+// left (causal backward, reverse forward).
 template <typename T, typename IdxT, bool BWD>
 static int launch_slab_aggregate(const T* a, const T* b, const IdxT* cu, int64_t S, int64_t C,
                                  int64_t L, bool r2l, const float* carry, float* agg,
                                  const Workspace& w, cudaStream_t s) {
   if (!agg || C <= 0 || L <= 0) return ASCAN_EINVAL;
-  // every row in parts of about kAggPart elements, so that the grid is many
-  // short waves of CTAs (a small tail) whatever the number of rows
-  int64_t splits = (L + slab::kAggPart / 2) / slab::kAggPart;
+  // one resident wave of CTAs (fewer when the rows are short: every warp
+  // gets at least one round of loads); each warp leaves one partial per row
+  // it touches, and a row spans at most ceil(warps / C) + 1 warps
+  constexpr int64_t kVec = 16 / static_cast<int64_t>(sizeof(T));
+  const int64_t sms = sm_count() > 0 ? sm_count() : 1;
+  const int64_t vectors = C * ((L + 2 * kVec - 2) / kVec);
+  int64_t ctas = sms * slab::kAggCtasPerSm;
+  const int64_t by_work = (vectors + slab::kAggMinShare * slab::kAggWarps - 1) /
+                          (slab::kAggMinShare * slab::kAggWarps);
+  if (ctas > by_work) ctas = by_work;
+  if (ctas < 1) ctas = 1;
   char* base = reinterpret_cast<char*>(w.ticket);
   const size_t counters_bytes = (static_cast<size_t>(C) * 4u + 15u) & ~static_cast<size_t>(15);
   const size_t room = w.clear_bytes > 256 + counters_bytes ? w.clear_bytes - 256 - counters_bytes : 0;
-  const int64_t by_room = static_cast<int64_t>(room / (8u * static_cast<size_t>(C)));
-  if (splits > by_room) splits = by_room;
-  if (splits < 1) splits = 1;
-  if (C * splits > 0x7fffffffll) return ASCAN_EINVAL;
+  const int64_t room_per_row = static_cast<int64_t>(room / (8u * static_cast<size_t>(C)));
+  int64_t per_row = (ctas * slab::kAggWarps + C - 1) / C + 1;
+  if (per_row > room_per_row) {
+    // fewer warps, as many as the partials' room allows, or whole rows per
+    // warp (per_row 0: no partials) when it holds fewer than two per row
+    const int64_t max_warps = room_per_row >= 2 ? (room_per_row - 1) * C : 0;
+    if (max_warps >= slab::kAggWarps) {
+      ctas = max_warps / slab::kAggWarps;
+      per_row = (ctas * slab::kAggWarps + C - 1) / C + 1;
+    } else {
+      per_row = 0;
+    }
+  }
   slab::AggArgs<T, IdxT> args{a, b, cu, S, L, C, carry, agg,
                               reinterpret_cast<uint32_t*>(base + 256),
                               reinterpret_cast<float2*>(base + 256 + counters_bytes),
-                              static_cast<uint32_t>(splits), g_err_host};
-  const dim3 grid(static_cast<unsigned>(C * splits)), block(slab::kAggThreads);
+                              static_cast<uint32_t>(per_row), g_err_host};
+  const dim3 grid(static_cast<unsigned>(ctas)), block(slab::kAggThreads);
   if (r2l)
     slab::slab_aggregate_kernel<T, IdxT, true, BWD><<<grid, block, 0, s>>>(args);
   else
@@ -1458,7 +1521,7 @@ static bool split_bidi(int cap, tma::TileSched& fs, tma::TileSched& bs, uint32_t
 // (wide tiles keep the order the narrow ones would have chosen).
 static tma::TileSched make_sched(int64_t kT, int64_t N, int64_t BL, int64_t S,
                                  bool allow_ragged, bool row_hint = false) {
-  tma::TileSched sch{static_cast<uint32_t>((N + kT - 1) / kT), 0u, 0u, 0u, 1u, 0u, 0u, 0u};
+  tma::TileSched sch{static_cast<uint32_t>((N + kT - 1) / kT), 0u, 0u, 0u, 1u, 0u, 0u, 0u, 1u};
   const int64_t C = BL > 0 ? N / BL : 0;
   const int mode = impl_mode();
   const int64_t per_row = BL > 0 ? (BL + kT - 1) / kT : 0;
@@ -1474,6 +1537,16 @@ static tma::TileSched make_sched(int64_t kT, int64_t N, int64_t BL, int64_t S,
     sch.stride = static_cast<uint32_t>(C);
     sch.ragged = aligned ? 0u : 1u;
     sch.num_tiles = static_cast<uint32_t>(C * per_row);
+    // Segment mode is offered when S sequences of equal length would each
+    // cover whole tiles; the kernels take it only if cu_seqlens really is
+    // that even split.  It moves a tile's predecessor from C to C * S
+    // tickets back: with C = 192 rows of 8 sequences of 65536 (one rank's
+    // share of B=8, T=65536, C=1536 on 8 GPUs) the row order puts it 1.3
+    // waves back and its carry arrives late (fwd 225 / bwd 422 us against
+    // 195 / 391 us for the same array with a sequence start at every tile).
+    if (aligned && S >= 2 && S + 1 <= tma::kCuCache && BL % S == 0 && (BL / S) % kT == 0 &&
+        C * S <= 0xffffffffll)
+      sch.segs = static_cast<uint32_t>(S);
   }
   return sch;
 }

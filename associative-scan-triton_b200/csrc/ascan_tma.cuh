@@ -217,6 +217,13 @@ struct StageMeta {
 //             tile-major across rows (tile j of every row, then tile j+1), so
 //             a tile's predecessor in its row is ticket - rows: many waves
 //             old when rows >> CTAs, and its status can be read ahead.
+//  segment mode (row mode with segs > 1): every row is also cut at its
+//             sequence starts into `segs` segments of equal length, a whole
+//             number of tiles each, and the (row, segment) pairs are the rows
+//             of the tile-major order: a segment's first tile starts a
+//             sequence, and a tile's predecessor is rows * segs tickets
+//             older.  Valid only when cu_seqlens[i] == i * BL / segs for
+//             every i, which the kernels check at start-up (seg_sched).
 struct TileSched {
   uint32_t num_tiles;
   uint32_t row_mode;
@@ -226,7 +233,20 @@ struct TileSched {
   uint32_t ragged;          // row mode with BL not a multiple of the tile (last tile of a row partial)
   uint32_t cta0;            // first CTA of this scan's group (0 unless bidirectional)
   uint32_t ctas;            // CTAs of the group (0: the whole grid)
+  uint32_t segs;            // segment mode if > 1 (and the start-up check passes)
 };
+
+// The schedule a launch runs: segment mode when the host offered it and
+// every thread's share of the cu_seqlens check held (`seg_ok`, voted by the
+// start-up barrier), else the plain row (or flat) order.
+__device__ __forceinline__ TileSched seg_sched(const TileSched& in, bool seg_ok) {
+  TileSched s = in;
+  if (s.segs > 1u && seg_ok)
+    s.stride = s.rows * s.segs;
+  else
+    s.segs = 1u;
+  return s;
+}
 
 // Hand-off slots between the consumer warps of one tile (no CTA barrier): the
 // per-warp totals and the tile's carry-in, each tagged with the tile's
@@ -444,6 +464,40 @@ __device__ __forceinline__ void read_block(const uint8_t* buf, const ThreadChunk
     for (int j = 0; j < P; ++j)
       v[j] = tile_elem<T, NIN>(buf, m, k, o + j, n_tma, n_valid, fill);
   }
+}
+
+// This thread's P elements [o, o+P) of 16-bit input k, packed two per word
+// (element 2i in the low half of w[i]); partial tiles pack the converted
+// elements back (exact: they came from T).
+template <typename T, int NIN, int P>
+__device__ __forceinline__ void read_block_packed(const uint8_t* buf, const ThreadChunks<T, P>& tc,
+                                                  const StageMeta<NIN, T, P>& m, int k, uint32_t o,
+                                                  uint32_t n_tma, uint32_t n_valid,
+                                                  uint32_t (&w)[P / 2]) {
+  static_assert(sizeof(T) == 2, "packed reads are for 16-bit types");
+  if (o + P <= n_tma) {
+#pragma unroll
+    for (int c = 0; c < ThreadChunks<T, P>::kChunks; ++c) {
+      const uint4 q = *reinterpret_cast<const uint4*>(buf + tc.off[c]);
+      w[4 * c] = q.x, w[4 * c + 1] = q.y, w[4 * c + 2] = q.z, w[4 * c + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < P / 2; ++i) {
+      const T lo = Cvt<T>::from(tile_elem<T, NIN>(buf, m, k, o + 2 * i, n_tma, n_valid, 0.f));
+      const T hi = Cvt<T>::from(tile_elem<T, NIN>(buf, m, k, o + 2 * i + 1, n_tma, n_valid, 0.f));
+      w[i] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+             (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+    }
+  }
+}
+
+// Element j of a packed block, as float (j is a compile-time index in the
+// unrolled loops that call this).
+template <typename T, int N>
+__device__ __forceinline__ float packed_elem(const uint32_t (&w)[N], int j) {
+  const uint16_t bits = static_cast<uint16_t>((j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xffffu));
+  return Cvt<T>::to(*reinterpret_cast<const T*>(&bits));
 }
 
 // This thread's 16 elements of a tile that starts `shift` elements into the

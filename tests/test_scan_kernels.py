@@ -465,6 +465,14 @@ TILE_ORDER_CASES = [
   (2, [100, 300, 12288]),             # positions before cu[0] lie in no sequence
   (7, [0, 1, 4097, 4098, 8192]),
   (160, [0, 4096 * 4]),
+  # equal sequences of whole tiles: the segment order (one row per
+  # (channel, sequence) pair)
+  (160, [0, 16384, 32768, 49152]),
+  # the same BL and S, but unequal sequences: the launch offers the segment
+  # order and the kernels' cu_seqlens check turns it down
+  (160, [0, 8192, 32768, 49152]),
+  (3, [0, 16384, 32768, 40960, 49152]),
+  (20, [0, 4096, 8192, 12288]),       # segments of one narrow tile each
 ]
 
 
@@ -501,6 +509,41 @@ def test_tile_orders_match_oracle(order, C, cu_list, dtype, reverse):
   assert_close_to_gold(dg, gdg, dtype, f"{order} dg", mask=mask)
   # positions outside every sequence are never written
   assert (y[:, ~mask[0]] == 7.0).all() and (dx[:, ~mask[0]] == 7.0).all()
+
+
+@pytest.mark.parametrize("width", [16, 32])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_segment_order_long_chains(width, dtype, reverse):
+  """One rank's share of the 8-GPU headline split, scaled down: 192 rows of
+  4 equal sequences of 32768 (segment order, a chain of 4 or 8 tiles per
+  segment, 768 segments over the SMs), forward and fused backward against the
+  oracle, and again with one sequence 4096 longer than the next, which the
+  kernels must scan in the plain row order."""
+  from associative_scan_triton import _lib
+  C, S, T = 192, 4, 32768
+  BL = S * T
+  g, x = make_inputs(C, BL, dtype=dtype, gate="verylong", seed=77)
+  dy = torch.randn(C, BL, generator=torch.Generator().manual_seed(8)).to(DEV, dtype)
+  for cu_list in ([i * T for i in range(S + 1)], [0, T + 4096, 2 * T, 3 * T, 4 * T]):
+    cu = torch.tensor(cu_list, dtype=torch.int32, device=DEV)
+    try:
+      _lib.set_tile_width(width)
+      y = torch.empty_like(x)
+      ast.forward_scan_full(g.clone(), x, cu, (S, 1, C), REVERSE=reverse, CHUNK_SIZE=2,
+                            TESTING=True, tokens_out=y)
+      dx, dg = torch.empty_like(x), torch.empty_like(x)
+      ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, (S, 1, C), CHUNK_SIZE=2,
+                                   CAUSAL=not reverse)
+      torch.cuda.synchronize()
+    finally:
+      _lib.set_tile_width(0)
+    _lib.check_device_error()
+    gold_y, _ = oracle.scan_fwd(g, x, cu, reverse=reverse)
+    assert_close_to_gold(y, gold_y, dtype, f"segment order y, cu={cu_list}")
+    gdx, gdg = oracle.scan_bwd(dy, g, y, cu, causal=not reverse)
+    assert_close_to_gold(dx, gdx, dtype, f"segment order dx, cu={cu_list}")
+    assert_close_to_gold(dg, gdg, dtype, f"segment order dg, cu={cu_list}")
 
 
 RAGGED_ROW_CASES = [
