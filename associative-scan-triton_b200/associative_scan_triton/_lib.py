@@ -33,6 +33,7 @@ ASCAN_OK = 0
 DEV_ERR_CU_END = 0x1
 DEV_ERR_CU_ORDER = 0x2
 DEV_ERR_LOOKBACK = 0x4
+DEV_ERR_EXCHANGE = 0x8
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 INDEX_CODES = {torch.int32: 0, torch.int64: 1}
@@ -49,6 +50,13 @@ EXPORTED_SYMBOLS = (
   "ascan_forward_slab",
   "ascan_backward_slab",
   "ascan_time_shard_fold",
+  "ascan_exchange_bytes",
+  "ascan_exchange_create",
+  "ascan_exchange_export",
+  "ascan_exchange_import",
+  "ascan_exchange_close",
+  "ascan_exchange_destroy",
+  "ascan_time_shard_exchange",
   "ascan_workspace_size_bidi",
   "ascan_forward_bidi",
   "ascan_backward_bidi",
@@ -98,6 +106,21 @@ def _bind(lib) -> None:
   lib.ascan_time_shard_fold.restype = ci
   lib.ascan_time_shard_fold.argtypes = [p, i64, ci, ci, i64, ctypes.c_uint32, ctypes.c_uint32, ci,
                                         p, p, p]
+  lib.ascan_exchange_bytes.restype = sz
+  lib.ascan_exchange_bytes.argtypes = [i64]
+  lib.ascan_exchange_create.restype = ci
+  lib.ascan_exchange_create.argtypes = [i64, ctypes.POINTER(p)]
+  lib.ascan_exchange_export.restype = ci
+  lib.ascan_exchange_export.argtypes = [p, p]
+  lib.ascan_exchange_import.restype = ci
+  lib.ascan_exchange_import.argtypes = [p, ctypes.POINTER(p)]
+  lib.ascan_exchange_close.restype = ci
+  lib.ascan_exchange_close.argtypes = [p]
+  lib.ascan_exchange_destroy.restype = ci
+  lib.ascan_exchange_destroy.argtypes = [p]
+  lib.ascan_time_shard_exchange.restype = ci
+  lib.ascan_time_shard_exchange.argtypes = [p, p, ci, ci, i64, i64, p, p, p, ci, ctypes.c_uint32,
+                                            ctypes.c_uint32, ci, ci, p, p, ctypes.c_longlong, p]
   lib.ascan_workspace_size_bidi.restype = sz
   lib.ascan_workspace_size_bidi.argtypes = [i64, i64, ci]
   lib.ascan_forward_bidi.restype = ci
@@ -211,6 +234,9 @@ def describe_device_error(code: int) -> str:
     parts.append("cu_seqlens is not monotone or lies outside [0, packed length]")
   if code & DEV_ERR_LOOKBACK:
     parts.append("a tile's predecessor did not publish within the bounded wait")
+  if code & DEV_ERR_EXCHANGE:
+    parts.append("a peer rank's time-shard record or release did not arrive within the "
+                 "bounded wait")
   return "; ".join(parts) or f"device error {code:#x}"
 
 
@@ -536,6 +562,93 @@ def time_shard_fold(records: torch.Tensor, world: int, rank: int, num_channels: 
       int(starts_new_mask), int(inner_boundary_mask), int(direction), carry, halo,
       _stream_ptr(device))
   _finish(rc, "ascan_time_shard_fold", device)
+
+
+IPC_HANDLE_BYTES = 64
+EXCHANGE_PUBLISH, EXCHANGE_FOLD, EXCHANGE_BOTH = 1, 2, 3
+
+
+def exchange_create(num_channels: int, device) -> int:
+  """ascan_exchange_create on ``device``: a zeroed exchange buffer (its
+  device address; free it with :func:`exchange_destroy`)."""
+  buf = ctypes.c_void_p(0)
+  with torch.cuda.device(torch.device(device)):
+    rc = load().ascan_exchange_create(int(num_channels), ctypes.byref(buf))
+  if rc != ASCAN_OK:
+    raise ScanError(f"ascan_exchange_create: {strerror(rc)}")
+  return int(buf.value)
+
+
+def exchange_export(buffer: int) -> bytes:
+  """The CUDA IPC handle of an exchange buffer of this process."""
+  h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+  rc = load().ascan_exchange_export(ctypes.c_void_p(buffer), h)
+  if rc != ASCAN_OK:
+    raise ScanError(f"ascan_exchange_export: {strerror(rc)}")
+  return h.raw
+
+
+def exchange_import(handle: bytes, device) -> int:
+  """Maps another process's exchange buffer on ``device``; its address here."""
+  if len(handle) != IPC_HANDLE_BYTES:
+    raise ValueError(f"an IPC handle has {IPC_HANDLE_BYTES} bytes, got {len(handle)}")
+  peer = ctypes.c_void_p(0)
+  with torch.cuda.device(torch.device(device)):
+    rc = load().ascan_exchange_import(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES),
+                                      ctypes.byref(peer))
+  if rc != ASCAN_OK:
+    raise ScanError(f"ascan_exchange_import: {strerror(rc)}")
+  return int(peer.value)
+
+
+def exchange_close(peer_buffer: int) -> None:
+  rc = load().ascan_exchange_close(ctypes.c_void_p(peer_buffer))
+  if rc != ASCAN_OK:
+    raise ScanError(f"ascan_exchange_close: {strerror(rc)}")
+
+
+def exchange_destroy(buffer: int) -> None:
+  rc = load().ascan_exchange_destroy(ctypes.c_void_p(buffer))
+  if rc != ASCAN_OK:
+    raise ScanError(f"ascan_exchange_destroy: {strerror(rc)}")
+
+
+def time_shard_exchange(buffer: int, buffers: torch.Tensor, world: int, rank: int,
+                        num_channels: int, aggregate: torch.Tensor | None,
+                        starts_new_mask: int, inner_boundary_mask: int, direction: int,
+                        mode: int, carry_out: torch.Tensor | None,
+                        halo_out: torch.Tensor | None = None, gates: torch.Tensor | None = None,
+                        states: torch.Tensor | None = None, timeout_s: float = 2.0) -> None:
+  """ascan_time_shard_exchange on the current stream of ``buffers``' device.
+  ``buffers``: int64 [world] device tensor of the exchange buffers as this
+  process addresses them (its own at ``rank``); ``aggregate`` [C, 2] float32;
+  ``gates``/``states`` [C, L] for the backward record's edge columns."""
+  _require_cuda("buffers", buffers, None)
+  device = buffers.device
+  if buffers.dtype != torch.int64 or buffers.numel() != world:
+    raise ValueError(f"buffers must be an int64 tensor of {world} addresses")
+  C = int(num_channels)
+  agg = _row_array("aggregate", aggregate, C, 2, device)
+  carry = _row_array("carry_out", carry_out, C, 2 if direction == 0 else 1, device)
+  halo = _row_array("halo_out", halo_out, C, 1, device)
+  L, dcode, gp, sp = 0, DTYPE_CODES[torch.float32], None, None
+  if direction == 1 and mode & EXCHANGE_PUBLISH:
+    for name, t in (("gates", gates), ("states", states)):
+      if t is None:
+        raise ValueError(f"the backward record needs {name}")
+      _require_cuda(name, t, device)
+      if t.dim() != 2 or t.shape[0] != C or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous [{C}, L] tensor")
+    if gates.shape != states.shape or gates.dtype != states.dtype:
+      raise ValueError("gates and states must have one shape and dtype")
+    L, dcode, gp, sp = int(gates.shape[1]), DTYPE_CODES[gates.dtype], gates.data_ptr(), \
+        states.data_ptr()
+  with torch.cuda.device(device):
+    rc = load().ascan_time_shard_exchange(
+      ctypes.c_void_p(buffer), buffers.data_ptr(), int(world), int(rank), C, L, agg, gp, sp,
+      dcode, int(starts_new_mask), int(inner_boundary_mask), int(direction), int(mode), carry,
+      halo, int(timeout_s * 1e9), _stream_ptr(device))
+  _finish(rc, "ascan_time_shard_exchange", device)
 
 
 def shift_pad(data: torch.Tensor, out: torch.Tensor, cu_seqlens: torch.Tensor,

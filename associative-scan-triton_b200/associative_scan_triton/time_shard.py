@@ -52,7 +52,7 @@ __all__ = [
   "SlabPlan", "plan_slabs", "even_bounds", "forward_carry", "backward_carry",
   "slab_forward_aggregate", "slab_forward", "slab_backward_aggregate", "slab_backward",
   "emulate_forward", "emulate_backward", "plan_masks", "fold_forward", "fold_backward",
-  "TimeShardStep", "scan_causal_time_sharded", "ScanCausalTimeShard",
+  "TimeShardStep", "scan_causal_time_sharded", "ScanCausalTimeShard", "PeerExchange",
 ]
 
 
@@ -263,38 +263,139 @@ def slab_backward(grad: torch.Tensor, gates: torch.Tensor, states: torch.Tensor,
 
 
 # ---------------------------------------------------------------------------
+# the exchange over peer memory (no collective)
+# ---------------------------------------------------------------------------
+
+class PeerExchange:
+  """One rank's side of the carry exchange over peer memory
+  (``ascan_time_shard_exchange``): its exchange buffer, the other ranks'
+  buffers mapped into this process through CUDA IPC, and a device table of
+  all of them.  :meth:`exchange` publishes this rank's record, waits for the
+  records its slab depends on and folds them into the carry in one kernel --
+  the all-gather and the fold of the collective path in one launch, with the
+  backward record's edge columns read straight from the slab's tensors.
+
+  :meth:`connect` is collective over a process group (one rank per GPU);
+  :meth:`emulated` builds every rank's side in one process on one device,
+  for tests (publish every rank, then fold every rank)."""
+
+  def __init__(self, num_channels: int, world: int, rank: int, device, own: int,
+               addresses: Sequence[int], mapped: Sequence[int] = ()):
+    self.C, self.world, self.rank = int(num_channels), int(world), int(rank)
+    self.device = torch.device(device)
+    self.own = int(own)
+    self.mapped = list(mapped)  # peers' buffers this process mapped (closed on close())
+    self.table = torch.tensor([int(a) for a in addresses], dtype=torch.int64, device=self.device)
+    self._open = True
+
+  @classmethod
+  def connect(cls, num_channels: int, device, group=None) -> "PeerExchange":
+    """Every rank of ``group`` creates its buffer; the IPC handles go round
+    with one ``all_gather_object`` and every rank maps the others' buffers."""
+    import torch.distributed as dist
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    device = torch.device(device)
+    own = _lib.exchange_create(num_channels, device)
+    handles: list = [None] * world
+    dist.all_gather_object(handles, _lib.exchange_export(own), group=group)
+    addresses, mapped = [], []
+    for j, h in enumerate(handles):
+      if j == rank:
+        addresses.append(own)
+      else:
+        peer = _lib.exchange_import(h, device)
+        mapped.append(peer)
+        addresses.append(peer)
+    return cls(num_channels, world, rank, device, own, addresses, mapped)
+
+  @classmethod
+  def emulated(cls, num_channels: int, world: int, device) -> list["PeerExchange"]:
+    """All ``world`` ranks' sides in this process on ``device``."""
+    bufs = [_lib.exchange_create(num_channels, device) for _ in range(world)]
+    return [cls(num_channels, world, k, device, bufs[k], bufs) for k in range(world)]
+
+  def exchange(self, direction: int, mode: int, masks: tuple[int, int],
+               aggregate: torch.Tensor | None, carry: torch.Tensor | None,
+               halo: torch.Tensor | None = None, gates: torch.Tensor | None = None,
+               states: torch.Tensor | None = None, timeout_s: float = 2.0) -> None:
+    """One exchange of ``direction`` (0 forward, 1 backward); ``mode``
+    ``_lib.EXCHANGE_PUBLISH``, ``_lib.EXCHANGE_FOLD`` or ``_lib.EXCHANGE_BOTH``."""
+    starts, inner = masks
+    _lib.time_shard_exchange(self.own, self.table, self.world, self.rank, self.C, aggregate,
+                             starts, inner, direction, mode, carry, halo, gates=gates,
+                             states=states, timeout_s=timeout_s)
+
+  def close(self, barrier: Callable[[], None] | None = None) -> None:
+    """Unmaps the peers' buffers, waits at ``barrier`` (every rank must have
+    unmapped this rank's buffer before it is freed) and frees this rank's."""
+    if not self._open:
+      return
+    self._open = False
+    torch.cuda.synchronize(self.device)
+    for peer in self.mapped:
+      _lib.exchange_close(peer)
+    if barrier is not None:
+      barrier()
+    _lib.exchange_destroy(self.own)
+
+
+# ---------------------------------------------------------------------------
 # single-process emulation: every slab on the current device, exchange = list
 # ---------------------------------------------------------------------------
 
 def emulate_forward(gates: Sequence[torch.Tensor], tokens: Sequence[torch.Tensor],
-                    plans: Sequence[SlabPlan]) -> list[torch.Tensor]:
+                    plans: Sequence[SlabPlan],
+                    peers: Sequence[PeerExchange] | None = None) -> list[torch.Tensor]:
   """The time-sharded forward of all slabs in one process: the same passes
   and device fold as the distributed driver; the exchange is writing every
-  slab's record into one ``[W, 2C]`` buffer."""
+  slab's record into one ``[W, 2C]`` buffer, or, with ``peers``
+  (:meth:`PeerExchange.emulated`), the peer-memory exchange kernel: every
+  rank publishes, then every rank folds."""
   C, W = gates[0].shape[0], len(plans)
   records = torch.empty(W, 2 * C, dtype=torch.float32, device=gates[0].device)
   for k, (g, x, p) in enumerate(zip(gates, tokens, plans)):
     slab_forward_aggregate(g, x, p, out=records[k].view(C, 2))
-  return [slab_forward(g, x, p, fold_forward(records, plans, k))
+  if peers is None:
+    carries = [fold_forward(records, plans, k) for k in range(W)]
+  else:
+    masks = plan_masks(plans)
+    carries = [torch.empty(C, 2, dtype=torch.float32, device=gates[0].device) for _ in range(W)]
+    for k in range(W):
+      peers[k].exchange(0, _lib.EXCHANGE_PUBLISH, masks, records[k].view(C, 2), None)
+    for k in range(W):
+      peers[k].exchange(0, _lib.EXCHANGE_FOLD, masks, None, carries[k])
+  return [slab_forward(g, x, p, carries[k])
           for k, (g, x, p) in enumerate(zip(gates, tokens, plans))]
 
 
 def emulate_backward(grads: Sequence[torch.Tensor], gates: Sequence[torch.Tensor],
-                     states: Sequence[torch.Tensor],
-                     plans: Sequence[SlabPlan]) -> list[tuple[torch.Tensor, torch.Tensor]]:
-  """The time-sharded backward of all slabs in one process."""
+                     states: Sequence[torch.Tensor], plans: Sequence[SlabPlan],
+                     peers: Sequence[PeerExchange] | None = None
+                     ) -> list[tuple[torch.Tensor, torch.Tensor]]:
+  """The time-sharded backward of all slabs in one process (``peers``: as in
+  :func:`emulate_forward`)."""
   C, W = gates[0].shape[0], len(plans)
-  records = torch.empty(W, 4 * C, dtype=torch.float32, device=gates[0].device)
-  zero = torch.zeros(C, dtype=torch.float32, device=gates[0].device)
+  device = gates[0].device
+  records = torch.empty(W, 4 * C, dtype=torch.float32, device=device)
+  zero = torch.zeros(C, dtype=torch.float32, device=device)
   for k, (dy, g, h, p) in enumerate(zip(grads, gates, states, plans)):
     slab_backward_aggregate(dy, g, h, p, out=records[k, :2 * C].view(C, 2), zero=zero)
-    records[k, 2 * C:3 * C].copy_(g[:, 0])
-    records[k, 3 * C:].copy_(h[:, -1])
-  out = []
-  for k, (dy, g, h, p) in enumerate(zip(grads, gates, states, plans)):
-    carry, halo = fold_backward(records, plans, k)
-    out.append(slab_backward(dy, g, h, p, carry, halo))
-  return out
+    if peers is None:
+      records[k, 2 * C:3 * C].copy_(g[:, 0])
+      records[k, 3 * C:].copy_(h[:, -1])
+  if peers is None:
+    folds = [fold_backward(records, plans, k) for k in range(W)]
+  else:
+    masks = plan_masks(plans)
+    folds = [(torch.empty(C, dtype=torch.float32, device=device),
+              torch.empty(C, dtype=torch.float32, device=device)) for _ in range(W)]
+    for k in range(W):
+      peers[k].exchange(1, _lib.EXCHANGE_PUBLISH, masks, records[k, :2 * C].view(C, 2), None,
+                        gates=gates[k], states=states[k])
+    for k in range(W):
+      peers[k].exchange(1, _lib.EXCHANGE_FOLD, masks, None, folds[k][0], halo=folds[k][1])
+  return [slab_backward(dy, g, h, p, folds[k][0], folds[k][1])
+          for k, (dy, g, h, p) in enumerate(zip(grads, gates, states, plans))]
 
 
 # ---------------------------------------------------------------------------
@@ -328,11 +429,18 @@ class TimeShardStep:
             of [4C] floats -> device fold -> seeded fused backward slab pass.
   Six kernels and two collectives per fwd+bwd, no host synchronisation, so a
   step can be captured in a CUDA graph.  ``gather(out, inp)`` defaults to
-  ``torch.distributed.all_gather_into_tensor`` on ``group``."""
+  ``torch.distributed.all_gather_into_tensor`` on ``group``.
+
+  ``exchange="peer"`` (every rank on one node, one GPU each) replaces each
+  direction's all-gather and fold -- and the backward's two column copies --
+  by one :class:`PeerExchange` kernel over NVLink peer memory: three kernels
+  per direction, no collective.  Call :meth:`close` (collective) before the
+  process group goes away."""
 
   def __init__(self, shape, dtype, plans: Sequence[SlabPlan], rank: int, device,
                group=None, gather: Callable[[torch.Tensor, torch.Tensor], None] | None = None,
-               allocate_outputs: bool = True):
+               allocate_outputs: bool = True, exchange: str = "nccl",
+               timeout_s: float = 2.0):
     C, L = (int(v) for v in shape)
     self.C, self.L, self.rank, self.world = C, L, rank, len(plans)
     self.plans, self.plan = list(plans), plans[rank]
@@ -356,12 +464,24 @@ class TimeShardStep:
       self.y = torch.empty(C, L, dtype=dtype, device=device)
       self.dx = torch.empty(C, L, dtype=dtype, device=device)
       self.dg = torch.empty(C, L, dtype=dtype, device=device)
+    if exchange not in ("nccl", "peer"):
+      raise ValueError(f"exchange must be 'nccl' or 'peer', got {exchange!r}")
+    self.exchange_kind, self.timeout_s, self.group = exchange, float(timeout_s), group
+    self.peer = PeerExchange.connect(C, device, group) if exchange == "peer" else None
     if gather is None:
       import torch.distributed as dist
 
       def gather(out, inp):
         dist.all_gather_into_tensor(out, inp, group=group)
     self._gather = gather
+
+  def close(self) -> None:
+    """Releases the peer exchange (collective over the group); a no-op for
+    the NCCL exchange."""
+    if self.peer is not None:
+      import torch.distributed as dist
+      self.peer.close(barrier=lambda: dist.barrier(group=self.group))
+      self.peer = None
 
   @staticmethod
   def _mark(marks):
@@ -381,10 +501,15 @@ class TimeShardStep:
     _lib.forward_slab(gates, tokens, None, None, cu, S, C, False,
                       row_aggregate=self.rec_f.view(C, 2))
     self._mark(marks)
-    self._gather(self.all_f, self.rec_f)
-    self._mark(marks)
-    starts, inner = self.masks
-    _lib.time_shard_fold(self.all_f, self.world, self.rank, C, starts, inner, 0, self.carry_f)
+    if self.peer is not None:  # exchange and fold in one kernel
+      self.peer.exchange(0, _lib.EXCHANGE_BOTH, self.masks, self.rec_f.view(C, 2), self.carry_f,
+                         timeout_s=self.timeout_s)
+      self._mark(marks)
+    else:
+      self._gather(self.all_f, self.rec_f)
+      self._mark(marks)
+      starts, inner = self.masks
+      _lib.time_shard_fold(self.all_f, self.world, self.rank, C, starts, inner, 0, self.carry_f)
     self._mark(marks)
     _lib.forward_slab(gates, tokens, y, None, cu, S, C, False, row_carry=self.carry_f)
     self._mark(marks)
@@ -404,14 +529,21 @@ class TimeShardStep:
       dx = torch.empty_like(grad)
     _lib.backward_slab(grad, gates, states, None, None, cu, S, C, True, row_carry=self.zero,
                        row_aggregate=self.rec_b[:2 * C].view(C, 2))
-    self.rec_b[2 * C:3 * C].copy_(gates[:, 0])
-    self.rec_b[3 * C:].copy_(states[:, -1])
-    self._mark(marks)
-    self._gather(self.all_b, self.rec_b)
-    self._mark(marks)
-    starts, inner = self.masks
-    _lib.time_shard_fold(self.all_b, self.world, self.rank, C, starts, inner, 1, self.carry_b,
-                         self.halo)
+    if self.peer is not None:  # edge columns, exchange and fold in one kernel
+      self._mark(marks)
+      self.peer.exchange(1, _lib.EXCHANGE_BOTH, self.masks, self.rec_b[:2 * C].view(C, 2),
+                         self.carry_b, halo=self.halo, gates=gates, states=states,
+                         timeout_s=self.timeout_s)
+      self._mark(marks)
+    else:
+      self.rec_b[2 * C:3 * C].copy_(gates[:, 0])
+      self.rec_b[3 * C:].copy_(states[:, -1])
+      self._mark(marks)
+      self._gather(self.all_b, self.rec_b)
+      self._mark(marks)
+      starts, inner = self.masks
+      _lib.time_shard_fold(self.all_b, self.world, self.rank, C, starts, inner, 1, self.carry_b,
+                           self.halo)
     self._mark(marks)
     _lib.backward_slab(grad, gates, states, dx, dg, cu, S, C, True, row_carry=self.carry_b,
                        row_state_halo=self.halo)

@@ -4,6 +4,8 @@
 // the units ascan_fwd_*.cu, ascan_bwd_*.cu, ascan_bidi.cu and ascan_misc.cu;
 // this file checks arguments, carves workspaces and dispatches on dtype and
 // index type (include/ascan.h documents every entry point).
+#include <cstring>
+
 #include "ascan_impl.cuh"
 
 namespace ascan {
@@ -24,6 +26,11 @@ int selftest_waits_run(void* workspace, long long limit_ns, long long* results, 
 int time_shard_fold_run(const float* records, int64_t record_floats, int world, int rank,
                         int64_t C, uint32_t new_mask, uint32_t inner_mask, int direction,
                         float* carry, float* halo, cudaStream_t s);
+int time_shard_exchange_run(void* own, const uint64_t* bufs, int world, int rank, int dir, int mode,
+                            int64_t C, int64_t L, const float* aggregate, const void* first,
+                            const void* last, int dtype, uint32_t new_mask, uint32_t inner_mask,
+                            float* carry, float* halo, unsigned long long timeout_ns,
+                            cudaStream_t s);
 
 }  // namespace ascan
 
@@ -186,6 +193,80 @@ int ascan_time_shard_fold(const float* records, int64_t record_floats, int world
   return time_shard_fold_run(records, record_floats, world, rank, num_channels, starts_new_mask,
                              inner_boundary_mask, direction, carry_out, halo_out,
                              static_cast<cudaStream_t>(stream));
+}
+
+// Exchange buffers of ascan_time_shard_exchange: a 512-byte header (epoch,
+// flag and consumed words per direction) and two directions x two slots of
+// 4 C floats.
+size_t ascan_exchange_bytes(int64_t num_channels) {
+  if (num_channels <= 0) return 0;
+  return 512 + 2 * 2 * 4 * static_cast<size_t>(num_channels) * sizeof(float);
+}
+
+int ascan_exchange_create(int64_t num_channels, void** buffer_out) {
+  if (!buffer_out || num_channels <= 0) return ASCAN_EINVAL;
+  *buffer_out = nullptr;
+  const size_t bytes = ascan_exchange_bytes(num_channels);
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return ASCAN_ECUDA;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(p);
+    return ASCAN_ECUDA;
+  }
+  *buffer_out = p;
+  return ASCAN_OK;
+}
+
+int ascan_exchange_export(void* buffer, void* handle_out) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == ASCAN_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!buffer || !handle_out) return ASCAN_EINVAL;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, buffer) != cudaSuccess) return ASCAN_ECUDA;
+  memcpy(handle_out, &h, sizeof(h));
+  return ASCAN_OK;
+}
+
+int ascan_exchange_import(const void* handle, void** peer_buffer_out) {
+  if (!handle || !peer_buffer_out) return ASCAN_EINVAL;
+  *peer_buffer_out = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return ASCAN_ECUDA;
+  *peer_buffer_out = p;
+  return ASCAN_OK;
+}
+
+int ascan_exchange_close(void* peer_buffer) {
+  if (!peer_buffer) return ASCAN_EINVAL;
+  return cudaIpcCloseMemHandle(peer_buffer) == cudaSuccess ? ASCAN_OK : ASCAN_ECUDA;
+}
+
+int ascan_exchange_destroy(void* buffer) {
+  if (!buffer) return ASCAN_EINVAL;
+  return cudaFree(buffer) == cudaSuccess ? ASCAN_OK : ASCAN_ECUDA;
+}
+
+int ascan_time_shard_exchange(void* buffer, const void* buffers, int world, int rank,
+                              int64_t num_channels, int64_t seq_total, const float* aggregate,
+                              const void* gates, const void* states, int dtype,
+                              uint32_t starts_new_mask, uint32_t inner_boundary_mask, int direction,
+                              int mode, float* carry_out, float* halo_out, long long timeout_ns,
+                              void* stream) {
+  if (!buffer || !buffers || world < 1 || world > 32 || rank < 0 || rank >= world ||
+      num_channels <= 0 || (direction != 0 && direction != 1) || mode < 1 || mode > 3 ||
+      timeout_ns <= 0)
+    return ASCAN_EINVAL;
+  if (dtype != ASCAN_F32 && dtype != ASCAN_F16 && dtype != ASCAN_BF16) return ASCAN_EINVAL;
+  if ((mode & 1) && !aggregate) return ASCAN_EINVAL;
+  if ((mode & 1) && direction == 1 && (!gates || !states || seq_total <= 0)) return ASCAN_EINVAL;
+  if ((mode & 2) && !carry_out) return ASCAN_EINVAL;
+  if (direction == 0 && halo_out) return ASCAN_EINVAL;
+  return time_shard_exchange_run(buffer, static_cast<const uint64_t*>(buffers), world, rank,
+                                 direction, mode, num_channels, seq_total, aggregate, gates,
+                                 states, dtype, starts_new_mask, inner_boundary_mask, carry_out,
+                                 halo_out, static_cast<unsigned long long>(timeout_ns),
+                                 static_cast<cudaStream_t>(stream));
 }
 
 // Workspace of a bidirectional pair: two halves, one per scan, each a

@@ -23,7 +23,9 @@ Secondary keys, each with its own fp64 parity check of a seeded sample of rows
   sequence_shard_configs2  configs[2] (varlen, C=2048, 32 seeded lengths, bf16)
                            split into whole-sequence shards across the ranks
   time_shard               configs[4] case 5b (C=256, one sequence of 2^20)
-                           time-sharded across the ranks (NCCL carry exchange)
+                           time-sharded across the ranks (carry exchange over
+                           NVLink peer memory, one kernel per direction)
+  time_shard_nccl          the same with the NCCL all-gather exchange (N > 1)
 and, on one GPU, a T sweep, the small-T graph replay, configs[3] and the CPU
 baseline.
 
@@ -521,10 +523,13 @@ def _sequence_shard_configs2(ast, dist, rank, world, device, steps, warmup) -> d
           "parity": _parity(dist, device, worst, checked, RTOL_HALF)}
 
 
-def _time_shard_5b(dist, rank: int, world: int, device, steps: int = 10) -> dict:
+def _time_shard_5b(dist, rank: int, world: int, device, steps: int = 10,
+                   exchange: str = "peer") -> dict:
   """configs[4]'s time-sharded case: C=256 channels of one sequence of T=2^20
   fp32 steps, gates ~ U(0.99, 1); rank k scans columns [kT/W, (k+1)T/W) and
-  exchanges per-row carries once per direction (NCCL).  At W=1 the same
+  exchanges per-row carries once per direction (``exchange``: "peer", one
+  kernel over NVLink peer memory that publishes, waits and folds; or "nccl",
+  an all-gather and a fold kernel).  At W=1 the same
   workload runs as an ordinary single-GPU scan.  Device time per fwd+bwd step,
   max over ranks; GB/s counts the single-device algorithmic bytes (32 B per
   element), so the second reads of the two passes show up as a lower rate.
@@ -553,8 +558,10 @@ def _time_shard_5b(dist, rank: int, world: int, device, steps: int = 10) -> dict
   g, x, dy = slab(99, "u"), slab(98, "n"), slab(97, "n")
   plans = ts.plan_slabs([0, TS_T], bounds)
   res = {}
+  step_obj = None
   if world > 1:
-    step_obj = ts.TimeShardStep(g.shape, g.dtype, plans, rank, device)
+    step_obj = ts.TimeShardStep(g.shape, g.dtype, plans, rank, device, exchange=exchange,
+                                timeout_s=10.0)
 
     def fwd():
       res["y"] = step_obj.forward(g, x)
@@ -590,10 +597,14 @@ def _time_shard_5b(dist, rank: int, world: int, device, steps: int = 10) -> dict
     step_obj.backward(dy, g, y_ph, marks=marks)
     h1 = time.perf_counter()
     torch.cuda.synchronize()
-    names = ["fwd_aggregate", "fwd_all_gather", "fwd_fold", "fwd_seeded",
-             "bwd_aggregate_and_edges", "bwd_all_gather", "bwd_fold", "bwd_seeded"]
+    if exchange == "peer":
+      names = ["fwd_aggregate", "fwd_exchange_and_fold", "fwd_none", "fwd_seeded",
+               "bwd_aggregate", "bwd_edges_exchange_and_fold", "bwd_none", "bwd_seeded"]
+    else:
+      names = ["fwd_aggregate", "fwd_all_gather", "fwd_fold", "fwd_seeded",
+               "bwd_aggregate_and_edges", "bwd_all_gather", "bwd_fold", "bwd_seeded"]
     phases = {n: round(_reduce(dist, 1e3 * a.elapsed_time(b), device), 1)
-              for n, a, b in zip(names, marks, marks[1:])}
+              for n, a, b in zip(names, marks, marks[1:]) if not n.endswith("_none")}
     phases["host_enqueue"] = round(_reduce(dist, 1e6 * (h1 - h0), device), 1)
     phases["unit"] = "us, max over ranks"
     try:
@@ -635,6 +646,8 @@ def _time_shard_5b(dist, rank: int, world: int, device, steps: int = 10) -> dict
   parity = _parity(dist, device, worst, len(rows) if rank == 0 else 0, RTOL_F32)
   n = TS_C * TS_T
   del graph  # released before the process group is destroyed
+  if step_obj is not None:
+    step_obj.close()  # collective: unmaps the peers' exchange buffers, frees this rank's
   del g, x, dy, res, pieces
   torch.cuda.empty_cache()
   out = {"workload": f"causal fwd+bwd, C={TS_C}, one sequence of T=2^20, fp32, "
@@ -646,7 +659,11 @@ def _time_shard_5b(dist, rank: int, world: int, device, steps: int = 10) -> dict
     out["phases_eager_step"] = phases
   return {**out,
           "gbs": round(STEP_BYTES_PER_ELEM * n / (step_ms * 1e-3) / 1e9, 1),
-          "exchange": ("one NCCL all-gather into a preallocated buffer per direction "
+          "exchange": ("one kernel per direction over NVLink peer memory (CUDA IPC): "
+                       "publishes this rank's [C,2] fwd / [C,4] bwd record, waits for the "
+                       "ranks it depends on, reads their records and folds the carry; no "
+                       "collective" if exchange == "peer" else
+                       "one NCCL all-gather into a preallocated buffer per direction "
                        "([C,2] fwd, [C,4] bwd floats per rank); carries folded on the device")
           if world > 1 else "none (single GPU)",
           "parity": parity}
@@ -867,7 +884,9 @@ def run_ours(args) -> tuple[dict | None, bool]:
                                                     min(args.steps, 50), 3)
     extra["sequence_shard_configs2"] = _sequence_shard_configs2(ast, dist, rank, world, device,
                                                                 min(args.steps, 20), 3)
-    extra["time_shard"] = _time_shard_5b(dist, rank, world, device)
+    extra["time_shard"] = _time_shard_5b(dist, rank, world, device, exchange="peer")
+    if world > 1:  # the same step with the collective exchange, for comparison
+      extra["time_shard_nccl"] = _time_shard_5b(dist, rank, world, device, exchange="nccl")
 
   if dist is not None:
     _barrier(dist, device)

@@ -63,6 +63,7 @@ enum ascan_status {
 #define ASCAN_DEV_ERR_CU_END 0x1u       /* cu_seqlens[num_seq] != seq_total */
 #define ASCAN_DEV_ERR_CU_ORDER 0x2u     /* cu_seqlens not monotone / out of [0, seq_total] */
 #define ASCAN_DEV_ERR_LOOKBACK 0x4u     /* a tile predecessor never published (bounded wait expired) */
+#define ASCAN_DEV_ERR_EXCHANGE 0x8u     /* a peer rank's record or release never came (bounded wait expired) */
 
 /* Library identification. */
 ASCAN_API int ascan_abi_version(void);
@@ -229,6 +230,52 @@ ASCAN_API int ascan_time_shard_fold(const float* records, int64_t record_floats,
                                     int rank, int64_t num_channels, uint32_t starts_new_mask,
                                     uint32_t inner_boundary_mask, int direction,
                                     float* carry_out, float* halo_out, void* stream);
+
+/*
+ * The same carry exchange without a collective (no counterpart in the
+ * reference): every rank owns an exchange buffer in its own device memory,
+ * maps the other ranks' buffers through CUDA IPC, and one kernel per
+ * direction publishes this rank's record in its buffer, waits for the records
+ * of the ranks its slab depends on and reads them over NVLink, folding them
+ * exactly as ascan_time_shard_fold does.
+ *
+ * ascan_exchange_bytes(C)         bytes of one exchange buffer
+ * ascan_exchange_create(C, &buf)  cudaMalloc + zero on the current device
+ * ascan_exchange_export(buf, h)   its IPC handle, ASCAN_IPC_HANDLE_BYTES bytes
+ * ascan_exchange_import(h, &peer) map another process's buffer (never this
+ *                                 process's own: use its pointer directly)
+ * ascan_exchange_close(peer)      unmap it
+ * ascan_exchange_destroy(buf)     free this process's buffer (every peer must
+ *                                 have closed its mapping first)
+ *
+ * ascan_time_shard_exchange: buffers = device array [world] of the buffers as
+ * this process addresses them (own buffer at `rank`); aggregate = this rank's
+ * [C][2] row_aggregate (ascan_forward_slab / ascan_backward_slab); gates and
+ * states ([C][seq_total], `dtype`) give the backward record's first gate and
+ * last state columns (direction 1; NULL for direction 0); masks, carry_out
+ * and halo_out as for ascan_time_shard_fold.  mode: 1 publish only, 2 wait
+ * and fold only, 3 both in one kernel (the normal case: one rank per GPU).
+ * Modes 1 then 2 let one process emulate all ranks on one device (publish
+ * every rank first, then fold every rank), so that no kernel waits for a
+ * kernel launched after it.  Every rank must run the same sequence of
+ * exchanges per direction.  Every wait gives up after timeout_ns
+ * (ASCAN_DEV_ERR_EXCHANGE); the kernel then completes and the stream stays
+ * usable.
+ */
+#define ASCAN_IPC_HANDLE_BYTES 64
+ASCAN_API size_t ascan_exchange_bytes(int64_t num_channels);
+ASCAN_API int ascan_exchange_create(int64_t num_channels, void** buffer_out);
+ASCAN_API int ascan_exchange_export(void* buffer, void* handle_out);
+ASCAN_API int ascan_exchange_import(const void* handle, void** peer_buffer_out);
+ASCAN_API int ascan_exchange_close(void* peer_buffer);
+ASCAN_API int ascan_exchange_destroy(void* buffer);
+ASCAN_API int ascan_time_shard_exchange(void* buffer, const void* buffers, int world, int rank,
+                                        int64_t num_channels, int64_t seq_total,
+                                        const float* aggregate, const void* gates,
+                                        const void* states, int dtype, uint32_t starts_new_mask,
+                                        uint32_t inner_boundary_mask, int direction, int mode,
+                                        float* carry_out, float* halo_out, long long timeout_ns,
+                                        void* stream);
 
 /*
  * Bidirectional pair in one launch: the causal scan of (gates_fwd,

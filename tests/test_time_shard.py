@@ -203,6 +203,76 @@ def _emulated_slabs_match_oracle(C, T, world, cu, dtype):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize(("C", "T", "world", "cu"), CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_peer_exchange_matches_collective_path(C, T, world, cu, dtype):
+  """The exchange over peer memory (every rank's side emulated in this
+  process: publish every rank, then fold every rank) gives the same carries,
+  so bit for bit the same slabs, as the gathered-records path -- over three
+  steps, so both record slots and the consumed-before-overwrite check are
+  used -- and both match the fp64 oracle."""
+  g, x = make_inputs(C, T, dtype=dtype, gate="verylong", seed=C + T + world)
+  dy = torch.randn(C, T, generator=torch.Generator().manual_seed(3)).to("cuda", dtype)
+  bounds = ts.even_bounds(T, world, align=64)
+  plans = ts.plan_slabs(cu, bounds)
+  sl = [slice(a, b) for a, b in zip(bounds, bounds[1:])]
+  gs = [g[:, s].contiguous() for s in sl]
+  xs = [x[:, s].contiguous() for s in sl]
+  dys = [dy[:, s].contiguous() for s in sl]
+  ref_y = ts.emulate_forward(gs, xs, plans)
+  ref_grads = ts.emulate_backward(dys, gs, ref_y, plans)
+  peers = ts.PeerExchange.emulated(C, world, "cuda")
+  try:
+    for _ in range(3):
+      ys = ts.emulate_forward(gs, xs, plans, peers=peers)
+      grads = ts.emulate_backward(dys, gs, ys, plans, peers=peers)
+      torch.cuda.synchronize()
+      for k in range(world):
+        assert torch.equal(ys[k], ref_y[k]), f"slab {k} y"
+        assert torch.equal(grads[k][0], ref_grads[k][0]), f"slab {k} dg"
+        assert torch.equal(grads[k][1], ref_grads[k][1]), f"slab {k} dx"
+  finally:
+    for p in peers:
+      p.close()
+  from associative_scan_triton import _lib
+  _lib.check_device_error()
+  cu_t = torch.tensor(cu, dtype=torch.int64, device="cuda")
+  gold_y, _ = oracle.scan_fwd(g, x, cu_t)
+  y = torch.cat(ys, dim=1)
+  assert_close_to_gold(y, gold_y, dtype, "peer-exchange y")
+  gdx, gdg = oracle.scan_bwd(dy, g, y, cu_t)
+  assert_close_to_gold(torch.cat([d[1] for d in grads], 1), gdx, dtype, "peer-exchange dx")
+  assert_close_to_gold(torch.cat([d[0] for d in grads], 1), gdg, dtype, "peer-exchange dg")
+
+
+@pytest.mark.gpu
+def test_peer_exchange_wait_gives_up():
+  """A fold whose predecessor never publishes (nothing ever sets its flag)
+  gives up after the bounded wait, reports ASCAN_DEV_ERR_EXCHANGE with the
+  missing rank, and leaves the context usable."""
+  from associative_scan_triton import _lib
+  C, world = 64, 2
+  _lib.clear_device_error()
+  peers = ts.PeerExchange.emulated(C, world, "cuda")
+  carry = torch.full((C, 2), 7.0, device="cuda")
+  try:
+    # rank 1's forward needs rank 0's record of exchange 0, which never comes
+    with pytest.raises(_lib.ScanError, match="peer rank"):
+      peers[1].exchange(0, _lib.EXCHANGE_FOLD, (0, 0), None, carry, timeout_s=0.05)
+      _lib.check_device_error()
+    code, _ = _lib.get_device_error()
+    assert code == 0  # raising cleared it
+    # the stream still works: a later publish + fold of the next exchange number
+    agg = torch.rand(C, 2, device="cuda")
+    peers[0].exchange(0, _lib.EXCHANGE_BOTH, (0, 0), agg, torch.empty(C, 2, device="cuda"))
+    torch.cuda.synchronize()
+  finally:
+    for p in peers:
+      p.close()
+    _lib.clear_device_error()
+
+
+@pytest.mark.gpu
 def test_slab_aggregate_matches_definition():
   C, T = 6, 4096 * 2 + 128
   g, x = make_inputs(C, T, gate="long", seed=11)
@@ -381,12 +451,15 @@ def test_slab_entry_points_refuse_unaligned_views():
 
 @pytest.mark.gpu
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_nccl_ranks_match_oracle(tmp_path):
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_nccl_ranks_match_oracle(tmp_path, exchange):
+  """One rank per GPU (2-4): the NCCL exchange, and the exchange kernel over
+  NVLink peer memory, against the fp64 oracle."""
   world = min(torch.cuda.device_count(), 4)
   script = REPO / "tests" / "time_shard_ranks.py"
   cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
          "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(script),
-         str(tmp_path)]
+         str(tmp_path), exchange]
   env = dict(os.environ, NCCL_NVLS_ENABLE="0")
   r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
   assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

@@ -1,10 +1,13 @@
-"""One rank of the NCCL time-shard test (launched by torch.distributed.run from
-tests/test_time_shard.py::test_nccl_ranks_match_oracle).
+"""One rank of the multi-GPU time-shard test (launched by
+torch.distributed.run from tests/test_time_shard.py::test_nccl_ranks_match_oracle).
 
-Every rank builds the same seeded global problem, keeps its slab, runs
-``scan_causal_time_sharded`` forward and backward (one exchange each over
-NCCL), and the slabs are gathered on rank 0, which checks them against the
-fp64 oracle on the whole axis and writes ``<out_dir>/ok``.
+Every rank builds the same seeded global problem and keeps its slab.  Mode
+``nccl`` runs ``scan_causal_time_sharded`` forward and backward (one exchange
+each over NCCL); mode ``peer`` runs three forward+backward steps of
+``TimeShardStep(exchange="peer")`` (the exchange kernel over NVLink peer
+memory) and checks that every step gives the same bits.  The slabs are
+gathered on rank 0, which checks them against the fp64 oracle on the whole
+axis and writes ``<out_dir>/ok``.
 """
 
 from __future__ import annotations
@@ -28,6 +31,7 @@ from associative_scan_triton import time_shard as ts  # noqa: E402
 
 def main() -> int:
   out_dir = Path(sys.argv[1])
+  mode = sys.argv[2] if len(sys.argv) > 2 else "nccl"
   rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
   local = int(os.environ.get("LOCAL_RANK", rank))
   torch.cuda.set_device(local)
@@ -41,11 +45,30 @@ def main() -> int:
   dy = torch.randn(C, T, generator=gen).cuda()
   bounds = ts.even_bounds(T, world, align=64)
   t0, t1 = bounds[rank], bounds[rank + 1]
-  gs = g[:, t0:t1].contiguous().requires_grad_(True)
-  xs = x[:, t0:t1].contiguous().requires_grad_(True)
-  y = ts.scan_causal_time_sharded(gs, xs, {"cu_seqlens": cu, "bounds": bounds, "group": None})
-  y.backward(dy[:, t0:t1].contiguous())
-  pieces = [y.detach(), xs.grad, gs.grad]
+  if mode == "peer":
+    plans = ts.plan_slabs(cu, bounds)
+    step = ts.TimeShardStep((C, t1 - t0), torch.float32, plans, rank, "cuda", exchange="peer",
+                            timeout_s=10.0)
+    gs, xs = g[:, t0:t1].contiguous(), x[:, t0:t1].contiguous()
+    dys = dy[:, t0:t1].contiguous()
+    runs = []
+    for _ in range(3):
+      y = step.forward(gs, xs).clone()
+      dg, dx = step.backward(dys, gs, y)
+      runs.append((y, dx.clone(), dg.clone()))
+    torch.cuda.synchronize()
+    from associative_scan_triton import _lib
+    _lib.check_device_error()
+    for r in runs[1:]:
+      assert all(torch.equal(a, b) for a, b in zip(r, runs[0])), "steps differ"
+    step.close()
+    pieces = list(runs[-1])
+  else:
+    gs = g[:, t0:t1].contiguous().requires_grad_(True)
+    xs = x[:, t0:t1].contiguous().requires_grad_(True)
+    y = ts.scan_causal_time_sharded(gs, xs, {"cu_seqlens": cu, "bounds": bounds, "group": None})
+    y.backward(dy[:, t0:t1].contiguous())
+    pieces = [y.detach(), xs.grad, gs.grad]
   gathered = []
   for piece in pieces:  # slabs may differ in length: pad to the longest
     width = max(b - a for a, b in zip(bounds, bounds[1:]))
@@ -61,10 +84,10 @@ def main() -> int:
     from scan_testlib import assert_close_to_gold
     cu_t = torch.tensor(cu, dtype=torch.int64)
     gold_y, _ = oracle.scan_fwd(g, x, cu_t)
-    assert_close_to_gold(gathered[0], gold_y, torch.float32, "nccl time-shard y")
+    assert_close_to_gold(gathered[0], gold_y, torch.float32, f"{mode} time-shard y")
     gdx, gdg = oracle.scan_bwd(dy, g, gathered[0], cu_t)
-    assert_close_to_gold(gathered[1], gdx, torch.float32, "nccl time-shard dx")
-    assert_close_to_gold(gathered[2], gdg, torch.float32, "nccl time-shard dg")
+    assert_close_to_gold(gathered[1], gdx, torch.float32, f"{mode} time-shard dx")
+    assert_close_to_gold(gathered[2], gdg, torch.float32, f"{mode} time-shard dg")
     (out_dir / "ok").write_text(str(world))
   return 0
 
