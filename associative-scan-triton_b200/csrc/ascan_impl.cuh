@@ -673,6 +673,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     const uint32_t ticket = m.ticket;
     if (ticket == kDone) break;
     const int64_t p0 = m.p0;
+    const int64_t row0 = IO ? m.row0 : 0, rt0 = IO ? m.t0 : 0;  // slab I/O: the tile's row and position
     const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
     const bool has_outside = m.has_outside != 0u;
     float a[kPerThread], b[kPerThread];
@@ -707,7 +708,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
       phase ^= 1u;
     }
     if (IO && args.io.carry != nullptr && head != 0u)
-      apply_row_carry<REV>(a, b, head, p0 + o, BL, args.io.carry);
+      apply_row_carry<REV>(a, b, head, RowPos(row0, rt0 + o, BL), BL, args.io.carry);
 
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(a, b, head), lane, ex, wtot);
@@ -717,7 +718,8 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
                                         err_host);
     // a, b hold the local prefixes: h = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV, P>(head);
-    if (IO && lastmask != 0u) record_row_agg<REV>(a, b, lastmask, cm, Pc, p0 + o, BL, args.io.agg);
+    if (IO && lastmask != 0u)
+      record_row_agg<REV>(a, b, lastmask, cm, Pc, RowPos(row0, rt0 + o, BL), BL, args.io.agg);
     if (__all_sync(kFull, cm == kThreadMask)) {  // warp-uniform: no lane holds a head
 #pragma unroll
       for (int j = 0; j < kPerThread; ++j) {
@@ -904,6 +906,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     const uint32_t ticket = m.ticket;
     if (ticket == kDone) break;
     const int64_t p0 = m.p0;
+    const int64_t row0 = IO ? m.row0 : 0, rt0 = IO ? m.t0 : 0;  // slab I/O: the tile's row and position
     const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
     const bool has_outside = m.has_outside != 0u;
     float dyv[kPerThread], gv[kPerThread];
@@ -997,10 +1000,10 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     // state neighbour from outside the slab, aggregate at the row's last element
     const uint32_t lastmask = IO && args.io.agg ? tail : 0u;
     if (IO && args.io.carry != nullptr && head != 0u)
-      apply_row_carry_adjoint<CAUSAL>(gv, dyv, head, p0 + o, BL, args.io.carry);
+      apply_row_carry_adjoint<CAUSAL>(gv, dyv, head, RowPos(row0, rt0 + o, BL), BL, args.io.carry);
     if constexpr (IO) {
       if (args.io.halo != nullptr && tail != 0u)
-        tail &= ~apply_row_halo<CAUSAL>(hv, tail, p0 + o, BL, args.io.halo);
+        tail &= ~apply_row_halo<CAUSAL>(hv, tail, RowPos(row0, rt0 + o, BL), BL, args.io.halo);
     }
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(gv, dyv, head), lane, ex, wtot);
@@ -1010,7 +1013,9 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
                                         err_host);
     // gv, dyv hold the local prefixes: dh = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV, P>(head);
-    if (IO && lastmask != 0u) record_row_agg<REV>(gv, dyv, lastmask, cm, Pc, p0 + o, BL, args.io.agg);
+    if (IO && lastmask != 0u)
+      record_row_agg<REV>(gv, dyv, lastmask, cm, Pc, RowPos(row0, rt0 + o, BL), BL,
+                          args.io.agg);
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
       const float d = ((cm >> j) & 1u) ? fmaf(gv[j], Pc.b, dyv[j]) : dyv[j];

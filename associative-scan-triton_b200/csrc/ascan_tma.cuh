@@ -192,6 +192,8 @@ struct StageMeta {
   uint32_t n_tma;      // tile elements covered by the TMA rows
   uint32_t has_outside;
   int64_t p0;          // flat index of the tile's first element
+  int64_t row0;        // its row
+  int64_t t0;          // its position in that row
   float halo[2];       // bwd: [0] gate neighbour, [1] state neighbour at the tile edge
   uint32_t halo_bulk;  // bit k: halo k is in halo_raw[k] instead of halo[k]
   uint32_t halo_idx[2];  // ragged rows: element of halo_raw[k] that is the neighbour
@@ -417,6 +419,8 @@ __device__ void build_meta(StageMeta<NIN, T, P>& m, const CuView<IdxT>& cu, int6
     m.n_valid = n_valid;
     m.n_tma = static_cast<uint32_t>(nt);
     m.p0 = p0;
+    m.row0 = (p0 - t0) / BL;
+    m.t0 = t0;
   }
 }
 
@@ -689,11 +693,25 @@ __device__ __forceinline__ uint32_t carry_mask(uint32_t head) {
 
 // ---- time slabs: per-row carry-in, halo and aggregate --------------------
 
-// Row index of flat position q when q sits at row position `want`, else -1.
-__device__ __forceinline__ int64_t row_at(int64_t q, int64_t BL, int64_t want) {
-  const int64_t r = q / BL;
-  return q - r * BL == want ? r : -1;
-}
+// Row and row position of a thread's first element, from its tile's row and
+// row position (t may run past the row end: the tile spans rows in flat
+// order).  The helpers below walk the thread's K elements from there by
+// increments -- no division on the consumers' path.
+struct RowPos {
+  int64_t r, t;
+  __device__ __forceinline__ RowPos(int64_t row0, int64_t t, int64_t BL) : r(row0), t(t) {
+    while (this->t >= BL) {
+      this->t -= BL;
+      ++r;
+    }
+  }
+  __device__ __forceinline__ void next(int64_t BL) {
+    if (++t == BL) {
+      t = 0;
+      ++r;
+    }
+  }
+};
 
 // Forward: the carried (gate product, state) of each row enters at the row's
 // first element in scan order, which is a sequence head: x' = x + g * state
@@ -701,16 +719,15 @@ __device__ __forceinline__ int64_t row_at(int64_t q, int64_t BL, int64_t want) {
 // products exactly.  `bits` holds the thread's heads.
 template <bool REV, int K>
 __device__ __forceinline__ void apply_row_carry(float (&a)[K], float (&b)[K], uint32_t bits,
-                                                int64_t p, int64_t BL, const float* carry) {
+                                                RowPos rp, int64_t BL, const float* carry) {
+  const int64_t want = REV ? BL - 1 : 0;
 #pragma unroll
   for (int j = 0; j < K; ++j) {
-    if ((bits >> j) & 1u) {
-      const int64_t r = row_at(p + j, BL, REV ? BL - 1 : 0);
-      if (r >= 0) {
-        b[j] = fmaf(a[j], carry[2 * r + 1], b[j]);
-        a[j] *= carry[2 * r];
-      }
+    if (((bits >> j) & 1u) && rp.t == want) {
+      b[j] = fmaf(a[j], carry[2 * rp.r + 1], b[j]);
+      a[j] *= carry[2 * rp.r];
     }
+    rp.next(BL);
   }
 }
 
@@ -720,17 +737,16 @@ __device__ __forceinline__ void apply_row_carry(float (&a)[K], float (&b)[K], ui
 // the element's own coefficient becomes the identity.
 template <bool CAUSAL, int K>
 __device__ __forceinline__ void apply_row_carry_adjoint(float (&a)[K], float (&b)[K],
-                                                        uint32_t bits, int64_t p, int64_t BL,
+                                                        uint32_t bits, RowPos rp, int64_t BL,
                                                         const float* carry) {
+  const int64_t want = CAUSAL ? BL - 1 : 0;
 #pragma unroll
   for (int j = 0; j < K; ++j) {
-    if ((bits >> j) & 1u) {
-      const int64_t r = row_at(p + j, BL, CAUSAL ? BL - 1 : 0);
-      if (r >= 0) {
-        b[j] += carry[r];
-        a[j] = 1.f;
-      }
+    if (((bits >> j) & 1u) && rp.t == want) {
+      b[j] += carry[rp.r];
+      a[j] = 1.f;
     }
+    rp.next(BL);
   }
 }
 
@@ -738,18 +754,17 @@ __device__ __forceinline__ void apply_row_carry_adjoint(float (&a)[K], float (&b
 // outside the slab.  Returns the bits that took a halo (their gate gradient
 // is not forced to zero).
 template <bool CAUSAL, int K>
-__device__ __forceinline__ uint32_t apply_row_halo(float (&hv)[K], uint32_t bits, int64_t p,
+__device__ __forceinline__ uint32_t apply_row_halo(float (&hv)[K], uint32_t bits, RowPos rp,
                                                    int64_t BL, const float* halo) {
+  const int64_t want = CAUSAL ? 0 : BL - 1;
   uint32_t used = 0u;
 #pragma unroll
   for (int j = 0; j < K; ++j) {
-    if ((bits >> j) & 1u) {
-      const int64_t r = row_at(p + j, BL, CAUSAL ? 0 : BL - 1);
-      if (r >= 0) {
-        hv[j] = halo[r];
-        used |= 1u << j;
-      }
+    if (((bits >> j) & 1u) && rp.t == want) {
+      hv[j] = halo[rp.r];
+      used |= 1u << j;
     }
+    rp.next(BL);
   }
   return used;
 }
@@ -760,17 +775,16 @@ __device__ __forceinline__ uint32_t apply_row_halo(float (&hv)[K], uint32_t bits
 template <bool REV, int K>
 __device__ __forceinline__ void record_row_agg(const float (&a)[K], const float (&b)[K],
                                                uint32_t bits, uint32_t cm, const Pfx& P,
-                                               int64_t p, int64_t BL, float* agg) {
+                                               RowPos rp, int64_t BL, float* agg) {
+  const int64_t want = REV ? 0 : BL - 1;
 #pragma unroll
   for (int j = 0; j < K; ++j) {
-    if ((bits >> j) & 1u) {
-      const int64_t r = row_at(p + j, BL, REV ? 0 : BL - 1);
-      if (r >= 0) {
-        const bool c = (cm >> j) & 1u;
-        agg[2 * r] = c ? a[j] * P.a : a[j];
-        agg[2 * r + 1] = c ? fmaf(a[j], P.b, b[j]) : b[j];
-      }
+    if (((bits >> j) & 1u) && rp.t == want) {
+      const bool c = (cm >> j) & 1u;
+      agg[2 * rp.r] = c ? a[j] * P.a : a[j];
+      agg[2 * rp.r + 1] = c ? fmaf(a[j], P.b, b[j]) : b[j];
     }
+    rp.next(BL);
   }
 }
 
