@@ -119,8 +119,9 @@ def _bind(lib) -> None:
   lib.ascan_exchange_destroy.restype = ci
   lib.ascan_exchange_destroy.argtypes = [p]
   lib.ascan_time_shard_exchange.restype = ci
-  lib.ascan_time_shard_exchange.argtypes = [p, p, ci, ci, i64, i64, p, p, p, ci, ctypes.c_uint32,
-                                            ctypes.c_uint32, ci, ci, p, p, ctypes.c_longlong, p]
+  lib.ascan_time_shard_exchange.argtypes = [p, p, ci, ci, i64, i64, ci, p, p, p, ci,
+                                            ctypes.c_uint32, ctypes.c_uint32, ci, ci, p, p,
+                                            ctypes.c_longlong, p]
   lib.ascan_workspace_size_bidi.restype = sz
   lib.ascan_workspace_size_bidi.argtypes = [i64, i64, ci]
   lib.ascan_forward_bidi.restype = ci
@@ -618,21 +619,24 @@ def time_shard_exchange(buffer: int, buffers: torch.Tensor, world: int, rank: in
                         starts_new_mask: int, inner_boundary_mask: int, direction: int,
                         mode: int, carry_out: torch.Tensor | None,
                         halo_out: torch.Tensor | None = None, gates: torch.Tensor | None = None,
-                        states: torch.Tensor | None = None, timeout_s: float = 2.0) -> None:
+                        states: torch.Tensor | None = None, timeout_s: float = 2.0,
+                        parts: int = 1) -> None:
   """ascan_time_shard_exchange on the current stream of ``buffers``' device.
   ``buffers``: int64 [world] device tensor of the exchange buffers as this
-  process addresses them (its own at ``rank``); ``aggregate`` [C, 2] float32;
-  ``gates``/``states`` [C, L] for the backward record's edge columns."""
+  process addresses them (its own at ``rank``); ``aggregate`` [parts * C, 2]
+  float32; ``gates``/``states`` [C, L] for the backward record's edge columns
+  (and, with ``parts`` > 1, the parts' edge columns); ``carry_out`` /
+  ``halo_out`` hold one entry per row part."""
   _require_cuda("buffers", buffers, None)
   device = buffers.device
   if buffers.dtype != torch.int64 or buffers.numel() != world:
     raise ValueError(f"buffers must be an int64 tensor of {world} addresses")
-  C = int(num_channels)
-  agg = _row_array("aggregate", aggregate, C, 2, device)
-  carry = _row_array("carry_out", carry_out, C, 2 if direction == 0 else 1, device)
-  halo = _row_array("halo_out", halo_out, C, 1, device)
+  C, H = int(num_channels), int(parts)
+  agg = _row_array("aggregate", aggregate, H * C, 2, device)
+  carry = _row_array("carry_out", carry_out, H * C, 2 if direction == 0 else 1, device)
+  halo = _row_array("halo_out", halo_out, H * C, 1, device)
   L, dcode, gp, sp = 0, DTYPE_CODES[torch.float32], None, None
-  if direction == 1 and mode & EXCHANGE_PUBLISH:
+  if direction == 1 and (mode & EXCHANGE_PUBLISH or H > 1):
     for name, t in (("gates", gates), ("states", states)):
       if t is None:
         raise ValueError(f"the backward record needs {name}")
@@ -645,7 +649,7 @@ def time_shard_exchange(buffer: int, buffers: torch.Tensor, world: int, rank: in
         states.data_ptr()
   with torch.cuda.device(device):
     rc = load().ascan_time_shard_exchange(
-      ctypes.c_void_p(buffer), buffers.data_ptr(), int(world), int(rank), C, L, agg, gp, sp,
+      ctypes.c_void_p(buffer), buffers.data_ptr(), int(world), int(rank), C, L, H, agg, gp, sp,
       dcode, int(starts_new_mask), int(inner_boundary_mask), int(direction), int(mode), carry,
       halo, int(timeout_s * 1e9), _stream_ptr(device))
   _finish(rc, "ascan_time_shard_exchange", device)

@@ -52,7 +52,7 @@ __all__ = [
   "SlabPlan", "plan_slabs", "even_bounds", "forward_carry", "backward_carry",
   "slab_forward_aggregate", "slab_forward", "slab_backward_aggregate", "slab_backward",
   "emulate_forward", "emulate_backward", "plan_masks", "fold_forward", "fold_backward",
-  "TimeShardStep", "scan_causal_time_sharded", "ScanCausalTimeShard", "PeerExchange",
+  "TimeShardStep", "scan_causal_time_sharded", "ScanCausalTimeShard", "PeerExchange", "row_parts",
 ]
 
 
@@ -317,13 +317,16 @@ class PeerExchange:
   def exchange(self, direction: int, mode: int, masks: tuple[int, int],
                aggregate: torch.Tensor | None, carry: torch.Tensor | None,
                halo: torch.Tensor | None = None, gates: torch.Tensor | None = None,
-               states: torch.Tensor | None = None, timeout_s: float = 2.0) -> None:
+               states: torch.Tensor | None = None, timeout_s: float = 2.0,
+               parts: int = 1) -> None:
     """One exchange of ``direction`` (0 forward, 1 backward); ``mode``
-    ``_lib.EXCHANGE_PUBLISH``, ``_lib.EXCHANGE_FOLD`` or ``_lib.EXCHANGE_BOTH``."""
+    ``_lib.EXCHANGE_PUBLISH``, ``_lib.EXCHANGE_FOLD`` or ``_lib.EXCHANGE_BOTH``;
+    ``parts`` > 1: the slab's rows were scanned as that many parts each
+    (:func:`row_parts`), one aggregate and one carry per part."""
     starts, inner = masks
     _lib.time_shard_exchange(self.own, self.table, self.world, self.rank, self.C, aggregate,
                              starts, inner, direction, mode, carry, halo, gates=gates,
-                             states=states, timeout_s=timeout_s)
+                             states=states, timeout_s=timeout_s, parts=parts)
 
   def close(self, barrier: Callable[[], None] | None = None) -> None:
     """Unmaps the peers' buffers, waits at ``barrier`` (every rank must have
@@ -337,6 +340,22 @@ class PeerExchange:
     if barrier is not None:
       barrier()
     _lib.exchange_destroy(self.own)
+
+
+def row_parts(num_channels: int, length: int, plan: SlabPlan, device,
+              waves: int = 4, tile: int = 8192) -> int:
+  """How many parts H to cut each row of a slab into for the peer exchange:
+  the smallest power of two with H * C rows filling ``waves`` waves of the
+  persistent kernels (one CTA per SM), so that in the seeded passes' tile
+  order a tile's predecessor is several waves older; 1 when the slab has a
+  sequence boundary inside or its parts would not be whole ``tile``s."""
+  if plan.inner_boundary:
+    return 1
+  sms = torch.cuda.get_device_properties(torch.device(device)).multi_processor_count
+  H = 1
+  while H * num_channels < waves * sms and length % (2 * H * tile) == 0:
+    H *= 2
+  return H
 
 
 # ---------------------------------------------------------------------------
@@ -468,6 +487,18 @@ class TimeShardStep:
       raise ValueError(f"exchange must be 'nccl' or 'peer', got {exchange!r}")
     self.exchange_kind, self.timeout_s, self.group = exchange, float(timeout_s), group
     self.peer = PeerExchange.connect(C, device, group) if exchange == "peer" else None
+    # peer exchange: every row scanned as H parts (one aggregate and one carry
+    # per part), so that the seeded passes see H times more rows
+    self.parts = row_parts(C, L, self.plan, device) if self.peer is not None else 1
+    H = self.parts
+    if H > 1:
+      self.cu_parts = torch.tensor([0, L // H], dtype=torch.int64, device=device)
+      self.agg_f = torch.empty(H * C, 2, **f32)
+      self.agg_b = torch.empty(H * C, 2, **f32)
+      self.carry_f = torch.empty(H * C, 2, **f32)
+      self.carry_b = torch.empty(H * C, **f32)
+      self.halo = torch.empty(H * C, **f32)
+      self.zero = torch.zeros(H * C, **f32)
     if gather is None:
       import torch.distributed as dist
 
@@ -498,6 +529,8 @@ class TimeShardStep:
     y = self.y if out is None else out
     if y is None:
       y = torch.empty_like(tokens)
+    if self.parts > 1:
+      return self._forward_parts(gates, tokens, y, marks)
     _lib.forward_slab(gates, tokens, None, None, cu, S, C, False,
                       row_aggregate=self.rec_f.view(C, 2))
     self._mark(marks)
@@ -527,6 +560,8 @@ class TimeShardStep:
       dg = torch.empty_like(gates)
     if dx is None:
       dx = torch.empty_like(grad)
+    if self.parts > 1:
+      return self._backward_parts(grad, gates, states, dg, dx, marks)
     _lib.backward_slab(grad, gates, states, None, None, cu, S, C, True, row_carry=self.zero,
                        row_aggregate=self.rec_b[:2 * C].view(C, 2))
     if self.peer is not None:  # edge columns, exchange and fold in one kernel
@@ -546,6 +581,45 @@ class TimeShardStep:
                            self.halo)
     self._mark(marks)
     _lib.backward_slab(grad, gates, states, dx, dg, cu, S, C, True, row_carry=self.carry_b,
+                       row_state_halo=self.halo)
+    self._mark(marks)
+    return dg, dx
+
+
+  def _views(self, *ts):
+    Cv, Lv = self.parts * self.C, self.L // self.parts
+    return [t.view(Cv, Lv) for t in ts]
+
+  def _forward_parts(self, gates, tokens, y, marks):
+    """Forward with every row cut into ``parts`` rows of L / parts columns
+    (the slab has no sequence boundary inside): the same three passes on the
+    [parts * C, L / parts] view; the exchange composes the parts' records and
+    hands back one carry per part."""
+    Cv = self.parts * self.C
+    gv, xv, yv = self._views(gates, tokens, y)
+    _lib.forward_slab(gv, xv, None, None, self.cu_parts, 1, Cv, False, row_aggregate=self.agg_f)
+    self._mark(marks)
+    self.peer.exchange(0, _lib.EXCHANGE_BOTH, self.masks, self.agg_f, self.carry_f,
+                       timeout_s=self.timeout_s, parts=self.parts)
+    self._mark(marks)
+    self._mark(marks)
+    _lib.forward_slab(gv, xv, yv, None, self.cu_parts, 1, Cv, False, row_carry=self.carry_f)
+    self._mark(marks)
+    return y
+
+  def _backward_parts(self, grad, gates, states, dg, dx, marks):
+    """Backward on the [parts * C, L / parts] view (see :meth:`_forward_parts`)."""
+    Cv = self.parts * self.C
+    dyv, gv, hv, dgv, dxv = self._views(grad, gates, states, dg, dx)
+    _lib.backward_slab(dyv, gv, hv, None, None, self.cu_parts, 1, Cv, True, row_carry=self.zero,
+                       row_aggregate=self.agg_b)
+    self._mark(marks)
+    self.peer.exchange(1, _lib.EXCHANGE_BOTH, self.masks, self.agg_b, self.carry_b,
+                       halo=self.halo, gates=gates, states=states, timeout_s=self.timeout_s,
+                       parts=self.parts)
+    self._mark(marks)
+    self._mark(marks)
+    _lib.backward_slab(dyv, gv, hv, dxv, dgv, self.cu_parts, 1, Cv, True, row_carry=self.carry_b,
                        row_state_halo=self.halo)
     self._mark(marks)
     return dg, dx

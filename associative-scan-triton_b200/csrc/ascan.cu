@@ -27,7 +27,7 @@ int time_shard_fold_run(const float* records, int64_t record_floats, int world, 
                         int64_t C, uint32_t new_mask, uint32_t inner_mask, int direction,
                         float* carry, float* halo, cudaStream_t s);
 int time_shard_exchange_run(void* own, const uint64_t* bufs, int world, int rank, int dir, int mode,
-                            int64_t C, int64_t L, const float* aggregate, const void* first,
+                            int64_t C, int64_t L, int parts, const float* aggregate, const void* first,
                             const void* last, int dtype, uint32_t new_mask, uint32_t inner_mask,
                             float* carry, float* halo, unsigned long long timeout_ns,
                             cudaStream_t s);
@@ -248,22 +248,29 @@ int ascan_exchange_destroy(void* buffer) {
 }
 
 int ascan_time_shard_exchange(void* buffer, const void* buffers, int world, int rank,
-                              int64_t num_channels, int64_t seq_total, const float* aggregate,
-                              const void* gates, const void* states, int dtype,
-                              uint32_t starts_new_mask, uint32_t inner_boundary_mask, int direction,
-                              int mode, float* carry_out, float* halo_out, long long timeout_ns,
-                              void* stream) {
+                              int64_t num_channels, int64_t seq_total, int parts,
+                              const float* aggregate, const void* gates, const void* states,
+                              int dtype, uint32_t starts_new_mask, uint32_t inner_boundary_mask,
+                              int direction, int mode, float* carry_out, float* halo_out,
+                              long long timeout_ns, void* stream) {
   if (!buffer || !buffers || world < 1 || world > 32 || rank < 0 || rank >= world ||
       num_channels <= 0 || (direction != 0 && direction != 1) || mode < 1 || mode > 3 ||
-      timeout_ns <= 0)
+      timeout_ns <= 0 || parts < 1)
     return ASCAN_EINVAL;
   if (dtype != ASCAN_F32 && dtype != ASCAN_F16 && dtype != ASCAN_BF16) return ASCAN_EINVAL;
-  if ((mode & 1) && !aggregate) return ASCAN_EINVAL;
-  if ((mode & 1) && direction == 1 && (!gates || !states || seq_total <= 0)) return ASCAN_EINVAL;
+  // parts > 1: the slab must have no sequence boundary inside, the parts are
+  // whole columns, and the fold needs the parts' aggregates (and columns)
+  if (parts > 1 && ((inner_boundary_mask >> rank) & 1u)) return ASCAN_EINVAL;
+  if (parts > 1 && direction == 1 && (seq_total <= 0 || seq_total % parts != 0))
+    return ASCAN_EINVAL;
+  const bool needs_aggregate = (mode & 1) || parts > 1;
+  const bool needs_columns = direction == 1 && ((mode & 1) || parts > 1);
+  if (needs_aggregate && !aggregate) return ASCAN_EINVAL;
+  if (needs_columns && (!gates || !states || seq_total <= 0)) return ASCAN_EINVAL;
   if ((mode & 2) && !carry_out) return ASCAN_EINVAL;
   if (direction == 0 && halo_out) return ASCAN_EINVAL;
   return time_shard_exchange_run(buffer, static_cast<const uint64_t*>(buffers), world, rank,
-                                 direction, mode, num_channels, seq_total, aggregate, gates,
+                                 direction, mode, num_channels, seq_total, parts, aggregate, gates,
                                  states, dtype, starts_new_mask, inner_boundary_mask, carry_out,
                                  halo_out, static_cast<unsigned long long>(timeout_ns),
                                  static_cast<cudaStream_t>(stream));

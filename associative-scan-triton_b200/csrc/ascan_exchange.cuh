@@ -84,12 +84,13 @@ struct XArgs {
   const uint64_t* bufs;      // [world] exchange buffers as this process maps them (own at rank)
   int world, rank, dir, mode;
   int64_t C, L;
-  const float* aggregate;    // [C][2] this rank's row aggregate (publish)
-  const T* first;            // backward publish: gates [C][L] (first column taken)
-  const T* last;             // backward publish: states [C][L] (last column taken)
+  int parts;                 // H: every row scanned as H parts of L / H columns
+  const float* aggregate;    // [H C][2] this rank's aggregate of every row part
+  const T* first;            // backward: gates [C][L] (the parts' first columns)
+  const T* last;             // backward: states [C][L] (the parts' last columns)
   uint32_t new_mask, inner_mask;
-  float* carry;              // fold: forward [C][2], backward [C]
-  float* halo;               // fold, backward: [C] or NULL
+  float* carry;              // fold: forward [H C][2], backward [H C]
+  float* halo;               // fold, backward: [H C] or NULL
   unsigned long long timeout_ns;
   uint32_t* err_host;
 };
@@ -116,11 +117,29 @@ __global__ void __launch_bounds__(kThreads) time_shard_exchange_kernel(const XAr
         report(ASCAN_DEV_ERR_EXCHANGE, (static_cast<unsigned long long>(tid) << 32) | e, a.err_host);
     }
     __syncthreads();
+    // the record of each row: its parts' aggregates composed in scan order
     float* slot = ring_slot(a.own, C, a.dir, e);
+    const int H = a.parts;
+    const int64_t lp = a.L / H;
     for (int64_t r = tid; r < C; r += kThreads) {
-      slot[2 * r] = a.aggregate[2 * r];
-      slot[2 * r + 1] = a.aggregate[2 * r + 1];
-      if (a.dir == 1) {
+      const float* ag = a.aggregate + 2 * H * r;
+      if (a.dir == 0) {  // h at the row end = P h_in + Y, part after part
+        float P = 1.f, Y = 0.f;
+        for (int k = 0; k < H; ++k) {
+          Y = fmaf(ag[2 * k], Y, ag[2 * k + 1]);
+          P *= ag[2 * k];
+        }
+        slot[2 * r] = P;
+        slot[2 * r + 1] = Y;
+      } else {  // dh at the row start = Q c_in + D, part after part from the right
+        float Q = ag[2 * (H - 1)], D = ag[2 * (H - 1) + 1];
+        for (int k = H - 2; k >= 0; --k) {
+          const float qg = ag[2 * k] * Cvt<T>::to(a.first[r * a.L + (k + 1) * lp]);
+          D = fmaf(qg, D, ag[2 * k + 1]);
+          Q *= qg;
+        }
+        slot[2 * r] = Q;
+        slot[2 * r + 1] = D;
         slot[2 * C + r] = Cvt<T>::to(a.first[r * a.L]);
         slot[3 * C + r] = Cvt<T>::to(a.last[r * a.L + a.L - 1]);
       }
@@ -167,8 +186,20 @@ __global__ void __launch_bounds__(kThreads) time_shard_exchange_kernel(const XAr
           }
         }
         const bool fresh = (a.new_mask >> rank) & 1u;
-        a.carry[2 * r] = fresh ? 1.f : prod;
-        a.carry[2 * r + 1] = fresh ? 0.f : state;
+        // the carry entering each part of the row (the parts continue one
+        // another: the slab has no sequence boundary inside when H > 1)
+        prod = fresh ? 1.f : prod;
+        state = fresh ? 0.f : state;
+        const float* ag = a.aggregate + 2 * a.parts * r;
+        float* out = a.carry + 2 * a.parts * r;
+        for (int k = 0; k < a.parts; ++k) {
+          out[2 * k] = prod;
+          out[2 * k + 1] = state;
+          if (k + 1 < a.parts) {
+            state = fmaf(ag[2 * k], state, ag[2 * k + 1]);
+            prod *= ag[2 * k];
+          }
+        }
       } else {
         float c = 0.f;
         // ranks world-1 down to rank+1, kGroup at a time
@@ -192,14 +223,23 @@ __global__ void __launch_bounds__(kThreads) time_shard_exchange_kernel(const XAr
             }
           }
         }
-        a.carry[r] = c;
+        // the carry entering each part's last column, from the right, and
+        // each part's state halo (the previous part's last state)
+        const int H = a.parts;
+        const int64_t lp = a.L / H;
+        const float* ag = a.aggregate + 2 * H * r;
+        for (int k = H - 1; k >= 0; --k) {
+          a.carry[H * r + k] = c;
+          if (k > 0) c = Cvt<T>::to(a.first[r * a.L + k * lp]) * fmaf(ag[2 * k], c, ag[2 * k + 1]);
+        }
         if (halo) {
           float h = 0.f;
           if (rank > 0 && !((a.new_mask >> rank) & 1u)) {
             const float* rec = ring_slot(reinterpret_cast<char*>(a.bufs[rank - 1]), C, 1, e);
             h = ld_relaxed_sys(rec + 3 * C + r);
           }
-          a.halo[r] = h;
+          a.halo[H * r] = h;
+          for (int k = 1; k < H; ++k) a.halo[H * r + k] = Cvt<T>::to(a.last[r * a.L + k * lp - 1]);
         }
       }
     }

@@ -673,7 +673,6 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     const uint32_t ticket = m.ticket;
     if (ticket == kDone) break;
     const int64_t p0 = m.p0;
-    const int64_t row0 = IO ? m.row0 : 0, rt0 = IO ? m.t0 : 0;  // slab I/O: the tile's row and position
     const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
     const bool has_outside = m.has_outside != 0u;
     float a[kPerThread], b[kPerThread];
@@ -701,14 +700,17 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     const uint32_t lastmask =
         IO && args.io.agg ? ((REV ? m.sbits[bit_word] : m.ebits[bit_word]) >> bit_shift) & kThreadMask
                           : 0u;
+    // time slabs: the row carry enters at the row's first element in scan
+    // order (read while the stage's metadata is still held: no register
+    // carries the tile's row through the scan)
+    if (IO && args.io.carry != nullptr && head != 0u)
+      apply_row_carry<REV>(a, b, head, RowPos(m.row0, m.t0 + o, BL), BL, args.io.carry);
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[stage]);
     if (++stage == NS) {
       stage = 0;
       phase ^= 1u;
     }
-    if (IO && args.io.carry != nullptr && head != 0u)
-      apply_row_carry<REV>(a, b, head, RowPos(row0, rt0 + o, BL), BL, args.io.carry);
 
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(a, b, head), lane, ex, wtot);
@@ -719,7 +721,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     // a, b hold the local prefixes: h = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV, P>(head);
     if (IO && lastmask != 0u)
-      record_row_agg<REV>(a, b, lastmask, cm, Pc, RowPos(row0, rt0 + o, BL), BL, args.io.agg);
+      record_row_agg<REV>(a, b, lastmask, cm, Pc, RowPos(p0 + o, BL), BL, args.io.agg);
     if (__all_sync(kFull, cm == kThreadMask)) {  // warp-uniform: no lane holds a head
 #pragma unroll
       for (int j = 0; j < kPerThread; ++j) {
@@ -906,7 +908,6 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     const uint32_t ticket = m.ticket;
     if (ticket == kDone) break;
     const int64_t p0 = m.p0;
-    const int64_t row0 = IO ? m.row0 : 0, rt0 = IO ? m.t0 : 0;  // slab I/O: the tile's row and position
     const uint32_t n_valid = m.n_valid, n_tma = m.n_tma;
     const bool has_outside = m.has_outside != 0u;
     float dyv[kPerThread], gv[kPerThread];
@@ -966,12 +967,6 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
                        !first_is_head && ticket >= sch.stride;
     uint4 early_raw = make_uint4(0u, 0u, 0u, 0u);
     if (early && lane == 0) early_raw = load_status_raw(args.st, ticket - sch.stride);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[stage]);
-    if (++stage == NS) {
-      stage = 0;
-      phase ^= 1u;
-    }
 
     // a[t] = g[t+1], hn[t] = h[t-1] (causal) or the mirror image (packed
     // states are shifted when they are unpacked)
@@ -999,11 +994,20 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     // time slabs: carried adjoint at the row's first element in scan order,
     // state neighbour from outside the slab, aggregate at the row's last element
     const uint32_t lastmask = IO && args.io.agg ? tail : 0u;
+    // (read while the stage's metadata is still held: no register carries the
+    // tile's row through the scan)
     if (IO && args.io.carry != nullptr && head != 0u)
-      apply_row_carry_adjoint<CAUSAL>(gv, dyv, head, RowPos(row0, rt0 + o, BL), BL, args.io.carry);
+      apply_row_carry_adjoint<CAUSAL>(gv, dyv, head, RowPos(m.row0, m.t0 + o, BL), BL,
+                                      args.io.carry);
     if constexpr (IO) {
       if (args.io.halo != nullptr && tail != 0u)
-        tail &= ~apply_row_halo<CAUSAL>(hv, tail, RowPos(row0, rt0 + o, BL), BL, args.io.halo);
+        tail &= ~apply_row_halo<CAUSAL>(hv, tail, RowPos(m.row0, m.t0 + o, BL), BL, args.io.halo);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[stage]);
+    if (++stage == NS) {
+      stage = 0;
+      phase ^= 1u;
     }
     Pfx ex, wtot;
     warp_scan<REV>(fold16_inplace<REV>(gv, dyv, head), lane, ex, wtot);
@@ -1014,8 +1018,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
     // gv, dyv hold the local prefixes: dh = A_loc * carry + B_loc before the first head
     const uint32_t cm = carry_mask<REV, P>(head);
     if (IO && lastmask != 0u)
-      record_row_agg<REV>(gv, dyv, lastmask, cm, Pc, RowPos(row0, rt0 + o, BL), BL,
-                          args.io.agg);
+      record_row_agg<REV>(gv, dyv, lastmask, cm, Pc, RowPos(p0 + o, BL), BL, args.io.agg);
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
       const float d = ((cm >> j) & 1u) ? fmaf(gv[j], Pc.b, dyv[j]) : dyv[j];

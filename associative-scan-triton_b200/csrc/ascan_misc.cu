@@ -80,13 +80,13 @@ int time_shard_fold_run(const float* records, int64_t record_floats, int world, 
 // The carry exchange of a time-sharded run over peer memory
 // (ascan_time_shard_exchange): one CTA on `s`.
 int time_shard_exchange_run(void* own, const uint64_t* bufs, int world, int rank, int dir, int mode,
-                            int64_t C, int64_t L, const float* aggregate, const void* first,
+                            int64_t C, int64_t L, int parts, const float* aggregate, const void* first,
                             const void* last, int dtype, uint32_t new_mask, uint32_t inner_mask,
                             float* carry, float* halo, unsigned long long timeout_ns,
                             cudaStream_t s) {
   auto launch = [&](auto tag) {
     using T = decltype(tag);
-    const xchg::XArgs<T> a{static_cast<char*>(own), bufs, world, rank, dir, mode, C, L, aggregate,
+    const xchg::XArgs<T> a{static_cast<char*>(own), bufs, world, rank, dir, mode, C, L, parts, aggregate,
                            static_cast<const T*>(first), static_cast<const T*>(last), new_mask,
                            inner_mask, carry, halo, timeout_ns, g_err_host};
     xchg::time_shard_exchange_kernel<T><<<1, xchg::kThreads, 0, s>>>(a);

@@ -705,6 +705,8 @@ struct RowPos {
       ++r;
     }
   }
+  // From a flat position (one division: for rare paths only).
+  __device__ __forceinline__ RowPos(int64_t p, int64_t BL) : r(p / BL), t(p - (p / BL) * BL) {}
   __device__ __forceinline__ void next(int64_t BL) {
     if (++t == BL) {
       t = 0;

@@ -253,7 +253,15 @@ ASCAN_API int ascan_time_shard_fold(const float* records, int64_t record_floats,
  * [C][2] row_aggregate (ascan_forward_slab / ascan_backward_slab); gates and
  * states ([C][seq_total], `dtype`) give the backward record's first gate and
  * last state columns (direction 1; NULL for direction 0); masks, carry_out
- * and halo_out as for ascan_time_shard_fold.  mode: 1 publish only, 2 wait
+ * and halo_out as for ascan_time_shard_fold.  parts = H > 1 (only for a slab
+ * with no sequence boundary inside, seq_total a multiple of H): the slab was
+ * scanned as [H C][seq_total / H] (every row cut into H parts), aggregate is
+ * [H C][2] (one record per part), the record sent is each row's parts
+ * composed, and carry_out ([H C][2] forward, [H C] backward) and halo_out
+ * ([H C]) hold one carry / halo per part -- so the seeded pass runs on the
+ * same [H C][seq_total / H] view, with H times more rows in its tile order.
+ * The fold then also needs aggregate and (backward) gates and states.
+ * mode: 1 publish only, 2 wait
  * and fold only, 3 both in one kernel (the normal case: one rank per GPU).
  * Modes 1 then 2 let one process emulate all ranks on one device (publish
  * every rank first, then fold every rank), so that no kernel waits for a
@@ -270,7 +278,7 @@ ASCAN_API int ascan_exchange_import(const void* handle, void** peer_buffer_out);
 ASCAN_API int ascan_exchange_close(void* peer_buffer);
 ASCAN_API int ascan_exchange_destroy(void* buffer);
 ASCAN_API int ascan_time_shard_exchange(void* buffer, const void* buffers, int world, int rank,
-                                        int64_t num_channels, int64_t seq_total,
+                                        int64_t num_channels, int64_t seq_total, int parts,
                                         const float* aggregate, const void* gates,
                                         const void* states, int dtype, uint32_t starts_new_mask,
                                         uint32_t inner_boundary_mask, int direction, int mode,

@@ -245,6 +245,122 @@ def test_peer_exchange_matches_collective_path(C, T, world, cu, dtype):
   assert_close_to_gold(torch.cat([d[0] for d in grads], 1), gdg, dtype, "peer-exchange dg")
 
 
+def _peer_parts_step(gs, xs, dys, plans, peers, H):
+  """One forward and backward of every slab through the peer exchange with
+  each row of a slab without inner boundaries scanned as H parts (the path
+  TimeShardStep(exchange="peer") takes): publish every rank, then fold every
+  rank, so no kernel waits for a later one."""
+  from associative_scan_triton import _lib
+  W, C = len(plans), gs[0].shape[0]
+  masks = ts.plan_masks(plans)
+  hs = [H if not p.inner_boundary else 1 for p in plans]
+  f32 = dict(dtype=torch.float32, device="cuda")
+
+  def views(k, *t):
+    return [u.view(hs[k] * C, u.shape[1] // hs[k]) for u in t]
+
+  def cu_of(k):
+    p = plans[k]
+    if hs[k] == 1:
+      return torch.tensor(p.local_cu, dtype=torch.int64, device="cuda")
+    return torch.tensor([0, p.length // hs[k]], dtype=torch.int64, device="cuda")
+
+  aggs = [torch.empty(hs[k] * C, 2, **f32) for k in range(W)]
+  carries = [torch.empty(hs[k] * C, 2, **f32) for k in range(W)]
+  for k in range(W):
+    gv, xv = views(k, gs[k], xs[k])
+    cu = cu_of(k)
+    _lib.forward_slab(gv, xv, None, None, cu, cu.numel() - 1, hs[k] * C, False, row_aggregate=aggs[k])
+  for k in range(W):
+    peers[k].exchange(0, _lib.EXCHANGE_PUBLISH, masks, aggs[k], None, parts=hs[k])
+  for k in range(W):
+    peers[k].exchange(0, _lib.EXCHANGE_FOLD, masks, aggs[k], carries[k], parts=hs[k])
+  ys = []
+  for k in range(W):
+    y = torch.empty_like(xs[k])
+    gv, xv, yv = views(k, gs[k], xs[k], y)
+    cu = cu_of(k)
+    _lib.forward_slab(gv, xv, yv, None, cu, cu.numel() - 1, hs[k] * C, False, row_carry=carries[k])
+    ys.append(y)
+  bags = [torch.empty(hs[k] * C, 2, **f32) for k in range(W)]
+  bcar = [torch.empty(hs[k] * C, **f32) for k in range(W)]
+  halos = [torch.empty(hs[k] * C, **f32) for k in range(W)]
+  for k in range(W):
+    dyv, gv, hv = views(k, dys[k], gs[k], ys[k])
+    cu = cu_of(k)
+    _lib.backward_slab(dyv, gv, hv, None, None, cu, cu.numel() - 1, hs[k] * C, True,
+                       row_carry=torch.zeros(hs[k] * C, **f32), row_aggregate=bags[k])
+  for k in range(W):
+    peers[k].exchange(1, _lib.EXCHANGE_PUBLISH, masks, bags[k], None, gates=gs[k], states=ys[k],
+                      parts=hs[k])
+  for k in range(W):
+    peers[k].exchange(1, _lib.EXCHANGE_FOLD, masks, bags[k], bcar[k], halo=halos[k], gates=gs[k],
+                      states=ys[k], parts=hs[k])
+  grads = []
+  for k in range(W):
+    dx, dg = torch.empty_like(xs[k]), torch.empty_like(xs[k])
+    dyv, gv, hv, dxv, dgv = views(k, dys[k], gs[k], ys[k], dx, dg)
+    cu = cu_of(k)
+    _lib.backward_slab(dyv, gv, hv, dxv, dgv, cu, cu.numel() - 1, hs[k] * C, True,
+                       row_carry=bcar[k], row_state_halo=halos[k])
+    grads.append((dg, dx))
+  return ys, grads
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H", [2, 4])
+@pytest.mark.parametrize(("C", "T", "world", "cu"), [
+  (8, 1 << 16, 4, [0, 1 << 16]),
+  (5, 3 * 4096 * 4, 4, [0, 5000, 12288, 20000, 49152]),  # inner boundaries: those slabs keep H=1
+  (3, 8192 * 8, 2, [0, 8192 * 4, 8192 * 8]),              # a slab starting a sequence
+])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_peer_exchange_row_parts_match_oracle(C, T, world, cu, H, dtype):
+  """Rows of a slab cut into H parts for the seeded passes: the exchange
+  composes the parts' records and returns one carry (and halo) per part; the
+  slabs match the fp64 oracle on the whole axis, over two steps."""
+  g, x = make_inputs(C, T, dtype=dtype, gate="verylong", seed=C + T + world + H)
+  dy = torch.randn(C, T, generator=torch.Generator().manual_seed(4)).to("cuda", dtype)
+  bounds = ts.even_bounds(T, world, align=64)
+  plans = ts.plan_slabs(cu, bounds)
+  sl = [slice(a, b) for a, b in zip(bounds, bounds[1:])]
+  gs = [g[:, s].contiguous() for s in sl]
+  xs = [x[:, s].contiguous() for s in sl]
+  dys = [dy[:, s].contiguous() for s in sl]
+  peers = ts.PeerExchange.emulated(C, world, "cuda")
+  try:
+    for _ in range(2):
+      ys, grads = _peer_parts_step(gs, xs, dys, plans, peers, H)
+    torch.cuda.synchronize()
+  finally:
+    for p in peers:
+      p.close()
+  from associative_scan_triton import _lib
+  _lib.check_device_error()
+  cu_t = torch.tensor(cu, dtype=torch.int64, device="cuda")
+  gold_y, _ = oracle.scan_fwd(g, x, cu_t)
+  y = torch.cat(ys, dim=1)
+  assert_close_to_gold(y, gold_y, dtype, f"row parts H={H} y")
+  gdx, gdg = oracle.scan_bwd(dy, g, y, cu_t)
+  assert_close_to_gold(torch.cat([d[1] for d in grads], 1), gdx, dtype, f"row parts H={H} dx")
+  assert_close_to_gold(torch.cat([d[0] for d in grads], 1), gdg, dtype, f"row parts H={H} dg")
+
+
+def test_row_parts_choice():
+  """H: a power of two filling four waves of rows, whole 8192-column parts,
+  1 for slabs with a boundary inside."""
+  import unittest.mock as um
+  props = um.Mock(multi_processor_count=148)
+  plan = ts.SlabPlan(0, 131072, (0, 131072), False, False)
+  with um.patch.object(torch.cuda, "get_device_properties", return_value=props):
+    assert ts.row_parts(256, 131072, plan, "cpu") == 4      # 1024 rows >= 592
+    assert ts.row_parts(1536, 131072, plan, "cpu") == 1
+    assert ts.row_parts(16, 131072, plan, "cpu") == 16      # capped by whole 8192-column parts
+    assert ts.row_parts(16, 8192 * 3, plan, "cpu") == 1
+    inner = ts.SlabPlan(0, 131072, (0, 5, 131072), False, True)
+    assert ts.row_parts(256, 131072, inner, "cpu") == 1
+
+
 @pytest.mark.gpu
 def test_peer_exchange_wait_gives_up():
   """A fold whose predecessor never publishes (nothing ever sets its flag)
