@@ -648,6 +648,29 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
             m.tail[0][e - n_tma] = Cvt<T>::to(args.g[p0 + e]);
             m.tail[1][e - n_tma] = Cvt<T>::to(args.x[p0 + e]);
           }
+          // time slabs: a row carry (gate product, state) that enters at the
+          // tile's first element in scan order becomes the tile's known
+          // carry-in -- the element stops being a head and the carry composes
+          // onto it exactly as the slab kernels' row carry does -- so the
+          // plain kernels serve seeded passes over rows of whole tiles
+          if (args.io.carry != nullptr) {
+            __syncwarp();  // every lane's boundary bits are in place
+            if (ln == 0) {
+              // (reverse order: only a full tile's last element is its first
+              // in scan order; a partial tile stays with the consumers)
+              const uint32_t e = REV ? n_valid - 1u : 0u;
+              const int64_t pos = m.t0 + e, q = pos / BL;
+              uint32_t& w = REV ? m.ebits[e >> 5] : m.sbits[e >> 5];
+              if (pos - q * BL == (REV ? BL - 1 : 0) && ((w >> (e & 31u)) & 1u) &&
+                  (!REV || n_valid == static_cast<uint32_t>(kTileElems))) {
+                const int64_t r = m.row0 + q;
+                m.te_raw[0] = __float_as_uint(args.io.carry[2 * r]);
+                m.te_raw[2] = __float_as_uint(args.io.carry[2 * r + 1]);
+                m.te_raw[1] = m.te_raw[3] = kStatusInclusive;
+                w &= ~(1u << (e & 31u));
+              }
+            }
+          }
         });
     return;
   }
@@ -881,6 +904,47 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
             if (bulk) mbar_expect_tx(bar, 16u * static_cast<uint32_t>(__popc(bulk)));
             if (bulk & (1u << kn)) bulk_load(m.halo_raw[kn], arr[kn] + bn, 16u, bar);
             if (bulk & (1u << kp)) bulk_load(m.halo_raw[kp], arr[kp] + bp, 16u, bar);
+          }
+          // time slabs: the row's carried adjoint term at the tile's first
+          // element in scan order becomes the tile's known carry-in (1, c)
+          // with that element's outside coefficient the identity; the row's
+          // state halo becomes the tile-edge state neighbour, and its element
+          // stops counting as a sequence start for the gate gradient.  (The
+          // launch takes this path only for rows of whole tiles, where both
+          // elements sit on a tile edge.)
+          if (args.io.carry != nullptr || args.io.halo != nullptr) {
+            __syncwarp();  // every lane's boundary bits are in place
+            if (ln == 0) {
+              if (args.io.carry != nullptr) {
+                // (causal: only a full tile's last element is its first in
+                // scan order; a partial tile stays with the consumers)
+                const uint32_t e = CAUSAL ? n_valid - 1u : 0u;
+                const int64_t pos = m.t0 + e, q = pos / BL;
+                uint32_t& w = CAUSAL ? m.ebits[e >> 5] : m.sbits[e >> 5];
+                if (pos - q * BL == (CAUSAL ? BL - 1 : 0) && ((w >> (e & 31u)) & 1u) &&
+                    (!CAUSAL || n_valid == static_cast<uint32_t>(kTileElems))) {
+                  m.te_raw[0] = __float_as_uint(1.f);
+                  m.te_raw[2] = __float_as_uint(args.io.carry[m.row0 + q]);
+                  m.te_raw[1] = m.te_raw[3] = kStatusInclusive;
+                  m.halo[0] = 1.f;  // the outside successor gate (already in c)
+                  m.halo_bulk &= ~1u;
+                  w &= ~(1u << (e & 31u));
+                }
+              }
+              if (args.io.halo != nullptr) {
+                const uint32_t e = CAUSAL ? 0u : n_valid - 1u;
+                const int64_t pos = m.t0 + e, q = pos / BL;
+                uint32_t& w = CAUSAL ? m.sbits[e >> 5] : m.ebits[e >> 5];
+                // (anti-causal: the neighbour of a partial tile's last element
+                // is not the tile-edge one, so that case stays with the consumers)
+                if (pos - q * BL == (CAUSAL ? 0 : BL - 1) && ((w >> (e & 31u)) & 1u) &&
+                    (CAUSAL || n_valid == static_cast<uint32_t>(kTileElems))) {
+                  m.halo[1] = args.io.halo[m.row0 + q];
+                  m.halo_bulk &= ~2u;
+                  w &= ~(1u << (e & 31u));
+                }
+              }
+            }
           }
         },
         IO && args.dx == nullptr ? 2 : NIN);  // aggregate-only: the states are never read
@@ -1650,7 +1714,12 @@ static int launch_fwd_tma_p(const FwdArgs<T, IdxT>& a, bool allow_ragged, bool i
     if (io) return 0;  // slab I/O exists in the staged kernels only
     return launch_fwd_tma_sched<T, IdxT, REV, GOUT, P, true>(a, sch, io, s);
   }
-  if constexpr (kStaged) return launch_fwd_tma_sched<T, IdxT, REV, GOUT, P, false>(a, sch, io, s);
+  // rows of whole tiles in row order, outputs written, no aggregate: the
+  // producers of the plain kernels turn the row carry into the tiles'
+  // carry-in, so the slab kernels (row I/O in the consumers) are not needed
+  const bool meta_io = io && sch.row_mode && !sch.ragged && a.io.agg == nullptr && a.y != nullptr;
+  if constexpr (kStaged)
+    return launch_fwd_tma_sched<T, IdxT, REV, GOUT, P, false>(a, sch, io && !meta_io, s);
   return 0;
 }
 
@@ -1710,7 +1779,12 @@ static int launch_bwd_tma_p(const BwdArgs<T, IdxT>& a, bool allow_ragged, bool i
     if (io) return 0;  // slab I/O exists in the staged kernels only
     return launch_bwd_tma_sched<T, IdxT, CAUSAL, P, true>(a, sch, io, s);
   }
-  if constexpr (kStaged) return launch_bwd_tma_sched<T, IdxT, CAUSAL, P, false>(a, sch, io, s);
+  // rows of whole tiles in row order, outputs written, no aggregate: the
+  // producers of the plain kernels carry the row I/O (see the forward)
+  const bool meta_io = io && sch.row_mode && !sch.ragged && a.io.agg == nullptr &&
+                       a.dx != nullptr;
+  if constexpr (kStaged)
+    return launch_bwd_tma_sched<T, IdxT, CAUSAL, P, false>(a, sch, io && !meta_io, s);
   return 0;
 }
 

@@ -875,7 +875,9 @@ __device__ __forceinline__ Pfx warp_tile_prefix(Sm& sm, uint32_t xi, Pfx thread_
                                                 int warp, int lane, bool& ok, uint32_t* err_host) {
   constexpr int kLast = kConsumerWarps - 1;
   const int lw = REV ? kLast - warp : warp;  // position of this warp in scan order
-  const bool need_lookback = !first_is_head && ticket >= stride;  // else a row's first tile
+  // a row's first tile has no predecessor, unless its carry-in was given with
+  // the tile (a time slab's row carry, te_known)
+  const bool need_lookback = !first_is_head && (ticket >= stride || te_known);
   XSlot& slot = sm.xs[xi];
   if (lane == 0) xs_put(&slot.warp[warp], warp_total, ticket);
   if (lw == 0 && need_lookback) {
