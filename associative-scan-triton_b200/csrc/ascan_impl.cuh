@@ -643,7 +643,7 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
     run_producer<T, IdxT, REV, NIN, NOUT, NS, P, RG>(
         sm, maps, cu, N, n_tma_total, sch, args.st, lane, err_host,
         [&](StageMeta<NIN, T, P>& m, int64_t p0, uint32_t n_tma, uint32_t n_valid, int ln,
-            uint64_t*) {
+            uint64_t* bar) {
           for (uint32_t e = n_tma + ln; e < n_valid; e += 32) {
             m.tail[0][e - n_tma] = Cvt<T>::to(args.g[p0 + e]);
             m.tail[1][e - n_tma] = Cvt<T>::to(args.x[p0 + e]);
@@ -664,8 +664,13 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
               if (pos - q * BL == (REV ? BL - 1 : 0) && ((w >> (e & 31u)) & 1u) &&
                   (!REV || n_valid == static_cast<uint32_t>(kTileElems))) {
                 const int64_t r = m.row0 + q;
-                m.te_raw[0] = __float_as_uint(args.io.carry[2 * r]);
-                m.te_raw[2] = __float_as_uint(args.io.carry[2 * r + 1]);
+                // the (product, state) pair comes with the tile when one
+                // 16-byte block holds it (the producer never waits on a load)
+                m.io_te = fetch_block(m.io_raw[0], args.io.carry, 2 * (N / BL), 2 * r, 2, bar);
+                if (m.io_te == 0u) {
+                  m.te_raw[0] = __float_as_uint(args.io.carry[2 * r]);
+                  m.te_raw[2] = __float_as_uint(args.io.carry[2 * r + 1]);
+                }
                 m.te_raw[1] = m.te_raw[3] = kStatusInclusive;
                 w &= ~(1u << (e & 31u));
               }
@@ -714,6 +719,8 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
         REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
     bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
     Pfx te_meta{__uint_as_float(m.te_raw[0]), __uint_as_float(m.te_raw[2]), kValid};
+    if (m.io_te != 0u)  // a time slab's row carry, fetched with the tile
+      te_meta = Pfx{m.io_raw[0][m.io_te - 1u], m.io_raw[0][m.io_te], kValid};
     // the scan-first warp re-reads its predecessor now, while it folds the tile
     const bool early = (REV ? kConsumerWarps - 1 - warp : warp) == 0 && !te_known &&
                        !first_is_head && ticket >= sch.stride;
@@ -923,8 +930,9 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
                 uint32_t& w = CAUSAL ? m.ebits[e >> 5] : m.sbits[e >> 5];
                 if (pos - q * BL == (CAUSAL ? BL - 1 : 0) && ((w >> (e & 31u)) & 1u) &&
                     (!CAUSAL || n_valid == static_cast<uint32_t>(kTileElems))) {
+                  m.io_te = fetch_block(m.io_raw[0], args.io.carry, N / BL, m.row0 + q, 1, bar);
                   m.te_raw[0] = __float_as_uint(1.f);
-                  m.te_raw[2] = __float_as_uint(args.io.carry[m.row0 + q]);
+                  if (m.io_te == 0u) m.te_raw[2] = __float_as_uint(args.io.carry[m.row0 + q]);
                   m.te_raw[1] = m.te_raw[3] = kStatusInclusive;
                   m.halo[0] = 1.f;  // the outside successor gate (already in c)
                   m.halo_bulk &= ~1u;
@@ -939,7 +947,8 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
                 // is not the tile-edge one, so that case stays with the consumers)
                 if (pos - q * BL == (CAUSAL ? 0 : BL - 1) && ((w >> (e & 31u)) & 1u) &&
                     (CAUSAL || n_valid == static_cast<uint32_t>(kTileElems))) {
-                  m.halo[1] = args.io.halo[m.row0 + q];
+                  m.io_halo = fetch_block(m.io_raw[1], args.io.halo, N / BL, m.row0 + q, 1, bar);
+                  if (m.io_halo == 0u) m.halo[1] = args.io.halo[m.row0 + q];
                   m.halo_bulk &= ~2u;
                   w &= ~(1u << (e & 31u));
                 }
@@ -1001,7 +1010,9 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
       halo_h = (m.halo_bulk & 2u) ? Cvt<T>::to(m.halo_raw[1][m.halo_idx[1]]) : m.halo[1];
     } else {  // aligned tiles: the neighbours sit at fixed places of their blocks
       halo_g = (m.halo_bulk & 1u) ? Cvt<T>::to(m.halo_raw[0][CAUSAL ? 0 : V - 1]) : m.halo[0];
-      halo_h = (m.halo_bulk & 2u) ? Cvt<T>::to(m.halo_raw[1][CAUSAL ? V - 1 : 0]) : m.halo[1];
+      halo_h = m.io_halo != 0u      ? m.io_raw[1][m.io_halo - 1u]  // a time slab's row halo
+               : (m.halo_bulk & 2u) ? Cvt<T>::to(m.halo_raw[1][CAUSAL ? V - 1 : 0])
+                                    : m.halo[1];
     }
     float g_nb, h_nb;
     if (CAUSAL) {
@@ -1026,6 +1037,7 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
         REV ? ((m.ebits[kBitWords - 1] >> 31) & 1u) != 0u : (m.sbits[0] & 1u) != 0u;
     bool te_known = m.te_raw[1] == kStatusInclusive && m.te_raw[3] == kStatusInclusive;
     Pfx te_meta{__uint_as_float(m.te_raw[0]), __uint_as_float(m.te_raw[2]), kValid};
+    if (m.io_te != 0u) te_meta.b = m.io_raw[0][m.io_te - 1u];  // a time slab's carried adjoint
     // the scan-first warp re-reads its predecessor now, while it folds the tile
     const bool early = (REV ? kConsumerWarps - 1 - warp : warp) == 0 && !te_known &&
                        !first_is_head && ticket >= sch.stride;

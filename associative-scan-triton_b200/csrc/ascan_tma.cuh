@@ -206,6 +206,11 @@ struct StageMeta {
   // copy together with the tile (all zero = unknown); an inclusive record in
   // it is the tile's carry-in
   alignas(16) uint32_t te_raw[4];
+  // time slabs in the plain kernels: 16-byte blocks of the row carry and row
+  // halo arrays, fetched by bulk copies with the tile; io_te / io_halo = 1 +
+  // the index of the row's value in its block (0: not fetched this way)
+  alignas(16) float io_raw[2][4];
+  uint32_t io_te, io_halo;
   alignas(16) uint32_t sbits[Geo<P>::kBitWords];  // sequence starts (and positions outside any sequence)
   alignas(16) uint32_t ebits[Geo<P>::kBitWords];  // sequence ends   (and positions outside any sequence)
   alignas(16) uint32_t obits[Geo<P>::kBitWords];  // positions outside any sequence (valid if has_outside)
@@ -421,6 +426,7 @@ __device__ void build_meta(StageMeta<NIN, T, P>& m, const CuView<IdxT>& cu, int6
     m.p0 = p0;
     m.row0 = (p0 - t0) / BL;
     m.t0 = t0;
+    m.io_te = m.io_halo = 0u;
   }
 }
 
@@ -714,6 +720,23 @@ struct RowPos {
     }
   }
 };
+
+// Fetches, with the stage's barrier, the 16-byte block of `arr` (`count`
+// floats) that holds arr[i .. i + n) into dst and returns 1 + the index of
+// arr[i] there, or 0 when no such block lies inside the array (the caller
+// then reads the values itself).  Producer lane only.
+__device__ __forceinline__ uint32_t fetch_block(float (&dst)[4], const float* arr, int64_t count,
+                                                int64_t i, int n, uint64_t* bar) {
+  const uintptr_t base = reinterpret_cast<uintptr_t>(arr);
+  const uintptr_t at = base + static_cast<uintptr_t>(4 * i);
+  const uintptr_t blk = at & ~static_cast<uintptr_t>(15);
+  if (blk < base || blk + 16 > base + static_cast<uintptr_t>(4 * count) ||
+      at + static_cast<uintptr_t>(4 * n) > blk + 16)
+    return 0u;
+  mbar_expect_tx(bar, 16u);
+  bulk_load(dst, reinterpret_cast<const void*>(blk), 16u, bar);
+  return 1u + static_cast<uint32_t>((at - blk) / 4);
+}
 
 // Forward: the carried (gate product, state) of each row enters at the row's
 // first element in scan order, which is a sequence head: x' = x + g * state
