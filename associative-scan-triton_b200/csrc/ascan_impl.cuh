@@ -492,12 +492,15 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, P, RG>&
   const uint32_t num_tiles = sch.num_tiles;
   // flat mode: row position of the current tile's first element, advanced by
   // the (constant) distance between this CTA's consecutive tiles
+  // (and its row, advanced the same way: no division per tile)
   const int64_t step = (static_cast<int64_t>(G) * kTileElems) % BL;
+  const int64_t row_step = (static_cast<int64_t>(G) * kTileElems) / BL;
   uint32_t ticket = blockIdx.x - sch.cta0;
-  int64_t t_flat = 0;
+  int64_t t_flat = 0, r_flat = 0;
   if (!sch.row_mode && ticket < num_tiles) {
     const uint32_t tile0 = REV ? num_tiles - 1u - ticket : ticket;
     t_flat = (static_cast<int64_t>(tile0) * kTileElems) % BL;
+    r_flat = (static_cast<int64_t>(tile0) * kTileElems) / BL;
   }
   uint32_t abort_seen = 0u;
   uint32_t iter = 0u;
@@ -528,7 +531,7 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, P, RG>&
       }
       break;
     }
-    int64_t p0, t0, limit;
+    int64_t p0, t0, limit, row0;
     if (sch.row_mode) {
       // stride = rows * segs: the (row, segment) pairs of one tile column
       const uint32_t j = ticket / sch.stride;
@@ -540,11 +543,13 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, P, RG>&
       t0 = static_cast<int64_t>(jj) * kTileElems;
       p0 = static_cast<int64_t>(c) * BL + t0;
       limit = static_cast<int64_t>(c) * BL + BL;
+      row0 = c;
     } else {
       const uint32_t tile = REV ? num_tiles - 1u - ticket : ticket;
       p0 = static_cast<int64_t>(tile) * kTileElems;
       t0 = t_flat;
       limit = N;
+      row0 = r_flat;
     }
     const int row = static_cast<int>(p0 / F::kElemsPerRow);
     constexpr uint32_t kBoxBytes = (F::kRows + (RG ? 1 : 0)) * 128u;
@@ -561,7 +566,7 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, P, RG>&
     }
     pending[stage] = true;
     last_parity[stage] = phase;
-    build_meta<IdxT, NIN, T, P>(m, cu, p0, t0, limit, n_tma_total, lane);
+    build_meta<IdxT, NIN, T, P>(m, cu, p0, t0, row0, limit, n_tma_total, lane);
     const int64_t rem = limit - p0;
     const uint32_t n_valid = static_cast<uint32_t>(rem < kTileElems ? rem : kTileElems);
     int64_t nt = n_tma_total - p0;
@@ -576,10 +581,12 @@ __device__ __forceinline__ void run_producer(tma::Smem<NIN, NOUT, NS, T, P, RG>&
     ticket += G;
     if (REV) {
       t_flat -= step;
-      if (t_flat < 0) t_flat += BL;
+      r_flat -= row_step;
+      if (t_flat < 0) t_flat += BL, --r_flat;
     } else {
       t_flat += step;
-      if (t_flat >= BL) t_flat -= BL;
+      r_flat += row_step;
+      if (t_flat >= BL) t_flat -= BL, ++r_flat;
     }
     abort_seen = __shfl_sync(kFull, abort_next, 0);
   }
@@ -659,9 +666,10 @@ __device__ __forceinline__ void fwd_tma_body(const CUtensorMap* map_g, const CUt
               // (reverse order: only a full tile's last element is its first
               // in scan order; a partial tile stays with the consumers)
               const uint32_t e = REV ? n_valid - 1u : 0u;
-              const int64_t pos = m.t0 + e, q = pos / BL;
+              int64_t pos = m.t0 + e, q = 0;
+              if (pos >= BL) q = pos / BL, pos -= q * BL;  // a tile that crosses a row end
               uint32_t& w = REV ? m.ebits[e >> 5] : m.sbits[e >> 5];
-              if (pos - q * BL == (REV ? BL - 1 : 0) && ((w >> (e & 31u)) & 1u) &&
+              if (pos == (REV ? BL - 1 : 0) && ((w >> (e & 31u)) & 1u) &&
                   (!REV || n_valid == static_cast<uint32_t>(kTileElems))) {
                 const int64_t r = m.row0 + q;
                 // the (product, state) pair comes with the tile when one
@@ -926,9 +934,10 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
                 // (causal: only a full tile's last element is its first in
                 // scan order; a partial tile stays with the consumers)
                 const uint32_t e = CAUSAL ? n_valid - 1u : 0u;
-                const int64_t pos = m.t0 + e, q = pos / BL;
+                int64_t pos = m.t0 + e, q = 0;
+                if (pos >= BL) q = pos / BL, pos -= q * BL;  // a tile that crosses a row end
                 uint32_t& w = CAUSAL ? m.ebits[e >> 5] : m.sbits[e >> 5];
-                if (pos - q * BL == (CAUSAL ? BL - 1 : 0) && ((w >> (e & 31u)) & 1u) &&
+                if (pos == (CAUSAL ? BL - 1 : 0) && ((w >> (e & 31u)) & 1u) &&
                     (!CAUSAL || n_valid == static_cast<uint32_t>(kTileElems))) {
                   m.io_te = fetch_block(m.io_raw[0], args.io.carry, N / BL, m.row0 + q, 1, bar);
                   m.te_raw[0] = __float_as_uint(1.f);
@@ -941,11 +950,12 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
               }
               if (args.io.halo != nullptr) {
                 const uint32_t e = CAUSAL ? 0u : n_valid - 1u;
-                const int64_t pos = m.t0 + e, q = pos / BL;
+                int64_t pos = m.t0 + e, q = 0;
+                if (pos >= BL) q = pos / BL, pos -= q * BL;  // a tile that crosses a row end
                 uint32_t& w = CAUSAL ? m.sbits[e >> 5] : m.ebits[e >> 5];
                 // (anti-causal: the neighbour of a partial tile's last element
                 // is not the tile-edge one, so that case stays with the consumers)
-                if (pos - q * BL == (CAUSAL ? 0 : BL - 1) && ((w >> (e & 31u)) & 1u) &&
+                if (pos == (CAUSAL ? 0 : BL - 1) && ((w >> (e & 31u)) & 1u) &&
                     (CAUSAL || n_valid == static_cast<uint32_t>(kTileElems))) {
                   m.io_halo = fetch_block(m.io_raw[1], args.io.halo, N / BL, m.row0 + q, 1, bar);
                   if (m.io_halo == 0u) m.halo[1] = args.io.halo[m.row0 + q];

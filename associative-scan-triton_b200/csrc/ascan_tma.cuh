@@ -388,11 +388,11 @@ __device__ __forceinline__ void mark_segment(StageMeta<NIN, T, P>& m, const CuVi
 }
 
 // Builds the boundary bitmaps of the tile that starts at flat index p0, whose
-// first element sits at row position t0 and whose elements end at flat index
+// first element sits at row position t0 of row row0 and whose elements end at flat index
 // `limit` (the array end, or the row end in row mode).  Called by all lanes.
 template <typename IdxT, int NIN, typename T, int P>
 __device__ void build_meta(StageMeta<NIN, T, P>& m, const CuView<IdxT>& cu, int64_t p0, int64_t t0,
-                           int64_t limit, int64_t n_tma_total, int lane) {
+                           int64_t row0, int64_t limit, int64_t n_tma_total, int lane) {
   constexpr int kTileElems = Geo<P>::kTileElems, kBitWords = Geo<P>::kBitWords;
   const int64_t rem = limit - p0;  // elements of the tile that belong to it (row or array end)
   const uint32_t n_valid = static_cast<uint32_t>(rem < kTileElems ? rem : kTileElems);
@@ -424,7 +424,7 @@ __device__ void build_meta(StageMeta<NIN, T, P>& m, const CuView<IdxT>& cu, int6
     m.n_valid = n_valid;
     m.n_tma = static_cast<uint32_t>(nt);
     m.p0 = p0;
-    m.row0 = (p0 - t0) / BL;
+    m.row0 = row0;
     m.t0 = t0;
     m.io_te = m.io_halo = 0u;
   }
