@@ -5,7 +5,8 @@ Every rank builds the same seeded global problem and keeps its slab.  Mode
 ``nccl`` runs ``scan_causal_time_sharded`` forward and backward (one exchange
 each over NCCL); mode ``peer`` runs three forward+backward steps of
 ``TimeShardStep(exchange="peer")`` (the exchange kernel over NVLink peer
-memory) and checks that every step gives the same bits.  The slabs are
+memory) and checks that every step gives the same result (within fp32
+reassociation).  The slabs are
 gathered on rank 0, which checks them against the fp64 oracle on the whole
 axis and writes ``<out_dir>/ok``.
 """
@@ -59,8 +60,11 @@ def main() -> int:
     torch.cuda.synchronize()
     from associative_scan_triton import _lib
     _lib.check_device_error()
+    # every step the same result (within fp32 reassociation: a look-back
+    # composes predecessors in a timing-dependent order)
     for r in runs[1:]:
-      assert all(torch.equal(a, b) for a, b in zip(r, runs[0])), "steps differ"
+      for a, b in zip(r, runs[0]):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-5 * float(b.abs().max()))
     step.close()
     pieces = list(runs[-1])
   else:
