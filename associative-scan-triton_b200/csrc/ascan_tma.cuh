@@ -928,6 +928,18 @@ __device__ __forceinline__ Pfx warp_tile_prefix(Sm& sm, uint32_t xi, Pfx thread_
   Pfx te = pfx_empty();
   if (lw == kLast) {
     const Pfx tot = compose(wex, warp_total);
+    if (need_lookback && te_known && !(tot.f & kHead)) {
+      // The carry-in came with the tile (a row carry, or the predecessor's
+      // inclusive record): publish the inclusive record at once.  An
+      // aggregate would be wrong here, not just early: a row carry is in no
+      // earlier status slot, so a successor that composed this aggregate
+      // with the tiles before it (or with the empty prefix before ticket 0)
+      // would lose the carry.
+      const Pfx inc = compose(te_known_val, tot);
+      if (lane == 0) publish(st, ticket, kStatusInclusive, inc.a, inc.b);
+      ok = got && ok;  // got is warp-uniform
+      return compose(te_known_val, p_in);
+    }
     if (lane == 0) {
       const bool inclusive = (tot.f & kHead) || !need_lookback;
       publish(st, ticket, inclusive ? kStatusInclusive : kStatusAggregate, tot.a, tot.b);
@@ -942,8 +954,12 @@ __device__ __forceinline__ Pfx warp_tile_prefix(Sm& sm, uint32_t xi, Pfx thread_
       return compose(te, p_in);
     }
   }
-  if (need_lookback && __any_sync(kFull, !(p_in.f & kHead)))
-    got = xs_get_warp(&slot.te, true, ticket, te, &sm.abort) && got;
+  if (need_lookback && __any_sync(kFull, !(p_in.f & kHead))) {
+    if (te_known)  // warp-uniform; the scan-first warp posts this same value
+      te = te_known_val;
+    else
+      got = xs_get_warp(&slot.te, true, ticket, te, &sm.abort) && got;
+  }
   ok = got && ok;  // got is warp-uniform
   return compose(te, p_in);
 }

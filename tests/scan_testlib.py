@@ -61,10 +61,15 @@ def cu_of(seqlens, dtype=torch.int64, device="cuda") -> torch.Tensor:
 
 def make_inputs(C: int, BL: int, dtype=torch.float32, gate="uniform", seed=TEST_SEED,
                 device="cuda"):
-  """(gates, tokens) [C, BL]; gates U(0,1) / U(0.9,1) / sigmoid(N(2,1)), tokens N(0,1)."""
+  """(gates, tokens) [C, BL]; gates U(0,1) / U(0.9,1) / U(0.99,1) / sigmoid(N(2,1)), or
+  "nearone": 1 - 2^-8 with probability 0.02 and exactly 1 otherwise (exact in
+  every dtype; a 4096-element tile's gate product is about 0.73, so carries
+  reach across whole sequences); tokens N(0,1)."""
   gen = torch.Generator(device="cpu").manual_seed(seed)
   if gate == "uniform":
     g = torch.rand(C, BL, generator=gen)
+  elif gate == "nearone":
+    g = 1.0 - (torch.rand(C, BL, generator=gen) < 0.02).float() / 256
   elif gate == "long":
     g = 0.9 + 0.1 * torch.rand(C, BL, generator=gen)
   elif gate == "verylong":

@@ -9,7 +9,9 @@ import torch
 
 import associative_scan_triton as ast
 from oracle import oracle
-from scan_testlib import TEST_SEED, assert_close_to_gold, golden_cases, golden_tensor
+from scan_testlib import (
+  TEST_SEED, assert_close_to_gold, golden_cases, golden_tensor, make_inputs,
+)
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -57,6 +59,32 @@ def test_scan_bidirectional_branched_micro(chunk_size, num_channels, seqlen):
 
 def test_bidi_varlen_packed():
   _run(16, [5000, 33, 1, 4096, 700], 512, testing=False)
+
+
+@pytest.mark.parametrize("C", [8, 300])
+def test_bidi_long_memory(C):
+  """Both scans of the pair with gates of 1 or 1 - 2^-8 over sequences of many
+  tiles: a tile's gate product stays near 1, so a wrong carry would show on
+  whole tiles (row order for C = 300, flat order for C = 8)."""
+  seqlens = [40_000, 4096 * 6, 777]
+  cu = torch.tensor([0, *np.cumsum(seqlens)], device=DEV)
+  BL = int(cu[-1])
+  gf, xf = make_inputs(C, BL, gate="nearone", seed=C)
+  gb, xb = make_inputs(C, BL, gate="nearone", seed=C + 1)
+  leaves = [t.clone().requires_grad_(True) for t in (gf, xf, gb, xb)]
+  args = {"cu_seqlens": cu, "chunk_size": 512,
+          "grid": ast.get_grid(len(cu), max(seqlens), 512, C)}
+  yf, yb = ast.scan_bidirectional_branched(*leaves, args)
+  (yf.sum() + yb.sum()).backward()
+  ones = np.ones((C, BL))
+  oy_f, odx_f, odg_f = oracle.scan_fwd_bwd(gf, xf, ones, cu, causal=True)
+  oy_b, odx_b, odg_b = oracle.scan_fwd_bwd(gb, xb, ones, cu, causal=False)
+  assert_close_to_gold(yf, oy_f, torch.float32, "states fwd")
+  assert_close_to_gold(yb, oy_b, torch.float32, "states bwd")
+  assert_close_to_gold(leaves[0].grad, odg_f, torch.float32, "gates grad fwd")
+  assert_close_to_gold(leaves[1].grad, odx_f, torch.float32, "tokens grad fwd")
+  assert_close_to_gold(leaves[2].grad, odg_b, torch.float32, "gates grad bwd")
+  assert_close_to_gold(leaves[3].grad, odx_b, torch.float32, "tokens grad bwd")
 
 
 def test_bidi_matches_reference_golden():

@@ -632,6 +632,61 @@ def test_flat_sized_workspace_is_accepted(reverse):
   assert call(flat_bytes - 1) == -2  # ASCAN_EWORKSPACE: one byte short of the flat size
 
 
+LONG_MEMORY_CASES = [
+  # C, cu_seqlens
+  (300, [0, 4096 * 8]),                    # row order, more rows than CTAs
+  (5, [0, 4096 * 24]),                     # row order, fewer rows than CTAs
+  (3, [0, 16384, 32768, 49152]),           # segment order
+  (2, [0, 100_003]),                       # ragged rows
+  (40, [0, 3, 70_000, 70_001, 131_072]),   # boundaries inside
+]
+
+
+@pytest.mark.parametrize(("order", "width"), [
+  ("simple", 0), ("tma", 16), ("tma", 32), ("tma-row", 16), ("tma-row", 32),
+  ("tma-flat", 16), ("tma-flat", 32),
+])
+@pytest.mark.parametrize(("C", "cu_list"), LONG_MEMORY_CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_long_memory_gates(order, width, C, cu_list, dtype, reverse):
+  """Gates of exactly 1 or 1 - 2^-8: a tile's gate product stays near 1, so
+  every earlier tile of a sequence reaches its last element.  A carry put
+  together from the wrong look-back records then shows on the whole tile;
+  with gates below 0.99 a tile's product is under 1e-9 and such an error
+  would only touch its first few elements."""
+  from associative_scan_triton import _lib
+  BL = cu_list[-1]
+  S = len(cu_list) - 1
+  g, x = make_inputs(C, BL, dtype=dtype, gate="nearone", seed=C + S)
+  cu = torch.tensor(cu_list, dtype=torch.int64, device=DEV)
+  dy = torch.randn(C, BL, generator=torch.Generator().manual_seed(9)).to(DEV, dtype)
+  try:
+    _lib.set_implementation(order)
+    _lib.set_tile_width(width)
+    y, gp = torch.empty_like(x), g.clone()
+    ast.forward_scan_full(gp, x, cu, (S, 1, C), REVERSE=reverse, CHUNK_SIZE=2, TESTING=True,
+                          tokens_out=y)
+    y2 = torch.empty_like(x)
+    ast.forward_scan_full(g, x, cu, (S, 1, C), REVERSE=reverse, CHUNK_SIZE=2, TESTING=False,
+                          tokens_out=y2)
+    dx, dg = torch.empty_like(x), torch.empty_like(x)
+    ast.backward_scan_fused_full(dy, g, y, dx, dg, cu, (S, 1, C), CHUNK_SIZE=2,
+                                 CAUSAL=not reverse)
+    torch.cuda.synchronize()
+  finally:
+    _lib.set_tile_width(0)
+    _lib.set_implementation("auto")
+  _lib.check_device_error()
+  gold_y, gold_a = oracle.scan_fwd(g, x, cu, reverse=reverse)
+  assert_close_to_gold(y, gold_y, dtype, f"{order}/{width} y (gate-product launch)")
+  assert_close_to_gold(gp, gold_a, dtype, f"{order}/{width} gate products")
+  assert_close_to_gold(y2, gold_y, dtype, f"{order}/{width} y")
+  gdx, gdg = oracle.scan_bwd(dy, g, y, cu, causal=not reverse)
+  assert_close_to_gold(dx, gdx, dtype, f"{order}/{width} dx")
+  assert_close_to_gold(dg, gdg, dtype, f"{order}/{width} dg")
+
+
 WIDE_TILE_CASES = [
   # C, cu_seqlens: flat order, row order (aligned and ragged), look-back
   (64, [0, 8192 * 2]),

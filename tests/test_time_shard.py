@@ -516,6 +516,98 @@ def test_slab_aggregate_reduction_matches_definition(C, L, cu, dtype, with_carry
                                err_msg=f"backward aggregate causal={causal}")
 
 
+SEEDED_CASES = [
+  # rows of whole tiles, one sequence: row order, the producers inject the row I/O
+  (8, 49152, [0, 49152], [0, 16384, 32768, 49152]),
+  # equal sequences of whole tiles in every slab: segment order
+  (8, 49152, list(range(0, 49153, 8192)), [0, 16384, 32768, 49152]),
+  # a sequence start at a slab edge and one inside a slab
+  (8, 49152, [0, 16384, 20000, 49152], [0, 16384, 32768, 49152]),
+  # rows that are not whole tiles: the slab kernels (row I/O in the consumers)
+  (6, 15000, [0, 15000], [0, 5000, 10000, 15000]),
+  (6, 15000, [0, 4999, 5000, 5001, 15000], [0, 5000, 10000, 15000]),
+  # short sequences across the slab edges: flat order
+  (6, 49152, list(range(0, 49152, 96)) + [49152], [0, 16384, 32768, 49152]),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(("C", "L", "cu", "bounds"), SEEDED_CASES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("r2l", [False, True])
+@pytest.mark.parametrize("width", [0, 32])
+def test_seeded_slab_passes_match_whole_axis(C, L, cu, bounds, dtype, r2l, width):
+  """Every slab's forward (with the gate products) and backward, both scan
+  directions, seeded with the carry and state halo read off the fp64 oracle
+  of the whole axis, equals that oracle on the slab's columns.  The time
+  shard itself only runs the causal direction; the reverse forward and the
+  anti-causal backward take the same seeded paths with the row's first
+  element in scan order at the slab's right edge (forward) or left edge
+  (backward).  Width 32 forces the 8192-element tiles wherever they exist."""
+  from associative_scan_triton import _lib
+  _lib.set_tile_width(width)
+  try:
+    _seeded_slab_passes(C, L, cu, bounds, dtype, r2l)
+  finally:
+    _lib.set_tile_width(0)
+
+
+def _seeded_slab_passes(C, L, cu, bounds, dtype, r2l):
+  from associative_scan_triton import _lib
+  g, x = make_inputs(C, L, dtype=dtype, gate="long", seed=L + len(cu))
+  dy = torch.randn(C, L, generator=torch.Generator().manual_seed(7)).to("cuda", dtype)
+  # gates of 1 or 1 - 2^-8 (exact in every dtype): gate products over a whole
+  # slab stay far from underflow, so the carried product is checked too
+  gen = torch.Generator().manual_seed(11)
+  gp = (1.0 - (torch.rand(C, L, generator=gen) < 0.02).float() / 256).to("cuda", dtype)
+  y64, a64 = oracle.scan_fwd(g, x, cu, reverse=r2l)
+  yp64, ap64 = oracle.scan_fwd(gp, x, cu, reverse=r2l)
+  h = torch.from_numpy(y64).to("cuda", dtype)  # the states the backward reads
+  dx64, dg64 = oracle.scan_bwd(dy, g, h, cu, causal=not r2l)
+  g64, hq = g.double().cpu().numpy(), h.double().cpu().numpy()
+  starts = set(cu)  # columns where a sequence starts (and the axis end)
+  f32 = dict(dtype=torch.float32, device="cuda")
+  for k, p in enumerate(ts.plan_slabs(cu, bounds)):
+    a, b = p.t0, p.t1
+    sl = slice(a, b)
+    gs, xs, dys, hs = (t[:, sl].contiguous() for t in (g, x, dy, h))
+    lcu = torch.tensor(p.local_cu, dtype=torch.int64, device="cuda")
+    S = lcu.numel() - 1
+    # forward: the state and gate product just before the row's first
+    # element in scan order (column a - 1, or b for the reverse scan)
+    src = b if r2l else a - 1
+    linked = 0 <= src < L and (b if r2l else a) not in starts
+
+    def fwd_carry(yy, aa):
+      if linked:
+        return torch.tensor(np.stack([aa[:, src], yy[:, src]], 1), **f32)
+      return torch.tensor(np.stack([np.ones(C), np.zeros(C)], 1), **f32)
+
+    ys = torch.empty_like(xs)
+    _lib.forward_slab(gs, xs, ys, None, lcu, S, C, r2l, row_carry=fwd_carry(y64, a64))
+    assert_close_to_gold(ys, y64[:, sl], dtype, f"slab {k} states reverse={r2l}")
+    gps = gp[:, sl].contiguous()
+    ys2, gos = torch.empty_like(xs), torch.empty_like(xs)
+    _lib.forward_slab(gps, xs, ys2, gos, lcu, S, C, r2l, row_carry=fwd_carry(yp64, ap64))
+    assert_close_to_gold(ys2, yp64[:, sl], dtype, f"slab {k} states (gate output) reverse={r2l}")
+    assert_close_to_gold(gos, ap64[:, sl], dtype, f"slab {k} gate products reverse={r2l}")
+    # backward: the adjoint term from the column the adjoint comes from
+    # (b causal, a - 1 anti-causal) and the state neighbour on the other side
+    nb = a - 1 if r2l else b
+    if 0 <= nb < L and (a if r2l else b) not in starts:
+      bcarry = g64[:, nb] * dx64[:, nb]
+    else:
+      bcarry = np.zeros(C)
+    hn = b if r2l else a - 1
+    halo = hq[:, hn] if 0 <= hn < L and (b if r2l else a) not in starts else np.zeros(C)
+    dxs, dgs = torch.empty_like(xs), torch.empty_like(xs)
+    _lib.backward_slab(dys, gs, hs, dxs, dgs, lcu, S, C, not r2l,
+                       row_carry=torch.tensor(bcarry, **f32),
+                       row_state_halo=torch.tensor(halo, **f32))
+    assert_close_to_gold(dxs, dx64[:, sl], dtype, f"slab {k} d_tokens causal={not r2l}")
+    assert_close_to_gold(dgs, dg64[:, sl], dtype, f"slab {k} d_gates causal={not r2l}")
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize(("world", "cu"), [
   (2, [0, 512]), (4, [0, 512]), (4, [0, 100, 128, 300, 512]), (8, [0, 64, 65, 448, 512]),
