@@ -171,17 +171,20 @@ CASES = [
 @pytest.mark.parametrize("width", [0, 32])
 @pytest.mark.parametrize(("C", "T", "world", "cu"), CASES)
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_emulated_slabs_match_oracle(C, T, world, cu, dtype, width):
+@pytest.mark.parametrize("gate", ["verylong", "nearone"])
+def test_emulated_slabs_match_oracle(C, T, world, cu, dtype, width, gate):
+  """gate "nearone" keeps gate products near 1 over whole slabs, so every
+  slab's carry reaches the end of the axis."""
   from associative_scan_triton import _lib
   _lib.set_tile_width(width)  # 32: the slab kernels on 8192-element tiles
   try:
-    _emulated_slabs_match_oracle(C, T, world, cu, dtype)
+    _emulated_slabs_match_oracle(C, T, world, cu, dtype, gate)
   finally:
     _lib.set_tile_width(0)
 
 
-def _emulated_slabs_match_oracle(C, T, world, cu, dtype):
-  g, x = make_inputs(C, T, dtype=dtype, gate="verylong", seed=C + T + world)
+def _emulated_slabs_match_oracle(C, T, world, cu, dtype, gate):
+  g, x = make_inputs(C, T, dtype=dtype, gate=gate, seed=C + T + world)
   dy = torch.randn(C, T, generator=torch.Generator().manual_seed(3)).to("cuda", dtype)
   bounds = ts.even_bounds(T, world, align=64)
   plans = ts.plan_slabs(cu, bounds)
@@ -205,7 +208,8 @@ def _emulated_slabs_match_oracle(C, T, world, cu, dtype):
 @pytest.mark.gpu
 @pytest.mark.parametrize(("C", "T", "world", "cu"), CASES)
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_peer_exchange_matches_collective_path(C, T, world, cu, dtype):
+@pytest.mark.parametrize("gate", ["verylong", "nearone"])
+def test_peer_exchange_matches_collective_path(C, T, world, cu, dtype, gate):
   """The exchange over peer memory (every rank's side emulated in this
   process: publish every rank, then fold every rank) folds exactly the
   carries and halos of the gathered-records path, bit for bit, over three
@@ -215,7 +219,7 @@ def test_peer_exchange_matches_collective_path(C, T, world, cu, dtype):
   so two launches of one scan may differ in the last bits) and both match
   the fp64 oracle."""
   from associative_scan_triton import _lib
-  g, x = make_inputs(C, T, dtype=dtype, gate="verylong", seed=C + T + world)
+  g, x = make_inputs(C, T, dtype=dtype, gate=gate, seed=C + T + world)
   dy = torch.randn(C, T, generator=torch.Generator().manual_seed(3)).to("cuda", dtype)
   bounds = ts.even_bounds(T, world, align=64)
   plans = ts.plan_slabs(cu, bounds)
@@ -348,11 +352,12 @@ def _peer_parts_step(gs, xs, dys, plans, peers, H):
   (3, 8192 * 8, 2, [0, 8192 * 4, 8192 * 8]),              # a slab starting a sequence
 ])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_peer_exchange_row_parts_match_oracle(C, T, world, cu, H, dtype):
+@pytest.mark.parametrize("gate", ["verylong", "nearone"])
+def test_peer_exchange_row_parts_match_oracle(C, T, world, cu, H, dtype, gate):
   """Rows of a slab cut into H parts for the seeded passes: the exchange
   composes the parts' records and returns one carry (and halo) per part; the
   slabs match the fp64 oracle on the whole axis, over two steps."""
-  g, x = make_inputs(C, T, dtype=dtype, gate="verylong", seed=C + T + world + H)
+  g, x = make_inputs(C, T, dtype=dtype, gate=gate, seed=C + T + world + H)
   dy = torch.randn(C, T, generator=torch.Generator().manual_seed(4)).to("cuda", dtype)
   bounds = ts.even_bounds(T, world, align=64)
   plans = ts.plan_slabs(cu, bounds)
