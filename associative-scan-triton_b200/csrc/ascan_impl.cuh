@@ -924,9 +924,10 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
           // element in scan order becomes the tile's known carry-in (1, c)
           // with that element's outside coefficient the identity; the row's
           // state halo becomes the tile-edge state neighbour, and its element
-          // stops counting as a sequence start for the gate gradient.  (The
-          // launch takes this path only for rows of whole tiles, where both
-          // elements sit on a tile edge.)
+          // stops counting as a sequence start for the gate gradient.  (Only
+          // where that element sits on the tile's edge: always for rows of
+          // whole tiles, whose launches run the plain kernels; in the slab
+          // kernels the consumers handle the other tiles.)
           if (args.io.carry != nullptr || args.io.halo != nullptr) {
             __syncwarp();  // every lane's boundary bits are in place
             if (ln == 0) {
@@ -948,7 +949,10 @@ __device__ __forceinline__ void bwd_tma_body(const CUtensorMap* map_dy, const CU
                   w &= ~(1u << (e & 31u));
                 }
               }
-              if (args.io.halo != nullptr) {
+              // (not when the row aggregate is written: the slab kernels find
+              // the row's last element in scan order by this same boundary
+              // bit, so their consumers apply the halo themselves)
+              if (args.io.halo != nullptr && args.io.agg == nullptr) {
                 const uint32_t e = CAUSAL ? 0u : n_valid - 1u;
                 int64_t pos = m.t0 + e, q = 0;
                 if (pos >= BL) q = pos / BL, pos -= q * BL;  // a tile that crosses a row end

@@ -542,7 +542,8 @@ SEEDED_CASES = [
 @pytest.mark.parametrize("r2l", [False, True])
 @pytest.mark.parametrize("width", [0, 32])
 def test_seeded_slab_passes_match_whole_axis(C, L, cu, bounds, dtype, r2l, width):
-  """Every slab's forward (with the gate products) and backward, both scan
+  """Every slab's forward (alone, with the gate products, with the row
+  aggregate) and backward (alone, with the row aggregate), both scan
   directions, seeded with the carry and state halo read off the fp64 oracle
   of the whole axis, equals that oracle on the slab's columns.  The time
   shard itself only runs the causal direction; the reverse forward and the
@@ -596,6 +597,15 @@ def _seeded_slab_passes(C, L, cu, bounds, dtype, r2l):
     _lib.forward_slab(gps, xs, ys2, gos, lcu, S, C, r2l, row_carry=fwd_carry(yp64, ap64))
     assert_close_to_gold(ys2, yp64[:, sl], dtype, f"slab {k} states (gate output) reverse={r2l}")
     assert_close_to_gold(gos, ap64[:, sl], dtype, f"slab {k} gate products reverse={r2l}")
+    # states and the row aggregate in one pass (the slab kernels' record_row_agg)
+    carry_p = fwd_carry(yp64, ap64)
+    ys3, agg = torch.empty_like(xs), torch.empty(C, 2, **f32)
+    _lib.forward_slab(gps, xs, ys3, None, lcu, S, C, r2l, row_carry=carry_p, row_aggregate=agg)
+    assert_close_to_gold(ys3, yp64[:, sl], dtype, f"slab {k} states (with aggregate)")
+    want = _slab_agg_reference(gps.double().cpu().numpy(), xs.double().cpu().numpy(), p.local_cu,
+                               True, r2l, carry_p.double().cpu().numpy())
+    np.testing.assert_allclose(agg.cpu().numpy(), want, rtol=1e-4, atol=1e-5,
+                               err_msg=f"slab {k} forward aggregate reverse={r2l}")
     # backward: the adjoint term from the column the adjoint comes from
     # (b causal, a - 1 anti-causal) and the state neighbour on the other side
     nb = a - 1 if r2l else b
@@ -611,6 +621,16 @@ def _seeded_slab_passes(C, L, cu, bounds, dtype, r2l):
                        row_state_halo=torch.tensor(halo, **f32))
     assert_close_to_gold(dxs, dx64[:, sl], dtype, f"slab {k} d_tokens causal={not r2l}")
     assert_close_to_gold(dgs, dg64[:, sl], dtype, f"slab {k} d_gates causal={not r2l}")
+    dxs2, dgs2, bagg = torch.empty_like(xs), torch.empty_like(xs), torch.empty(C, 2, **f32)
+    _lib.backward_slab(dys, gs, hs, dxs2, dgs2, lcu, S, C, not r2l,
+                       row_carry=torch.tensor(bcarry, **f32),
+                       row_state_halo=torch.tensor(halo, **f32), row_aggregate=bagg)
+    assert_close_to_gold(dxs2, dx64[:, sl], dtype, f"slab {k} d_tokens (with aggregate)")
+    assert_close_to_gold(dgs2, dg64[:, sl], dtype, f"slab {k} d_gates (with aggregate)")
+    want = _slab_agg_reference(gs.double().cpu().numpy(), dys.double().cpu().numpy(), p.local_cu,
+                               False, not r2l, np.asarray(bcarry, dtype=np.float32).astype(np.float64))
+    np.testing.assert_allclose(bagg.cpu().numpy(), want, rtol=1e-4, atol=1e-5,
+                               err_msg=f"slab {k} backward aggregate causal={not r2l}")
 
 
 @pytest.mark.gpu
