@@ -155,6 +155,75 @@ def test_exchange_and_folds_on_gloo_ranks(world, cu):
   assert not errors and all(p.exitcode == 0 for p in procs), errors
 
 
+SLAB_CONTRACT_CASES = [
+  ([0, 600], [0, 200, 400, 600]),
+  ([0, 200, 250, 600], [0, 200, 400, 600]),        # a start on a slab edge, one inside
+  (list(range(0, 600, 48)) + [600], [0, 200, 400, 600]),
+  ([0, 1, 199, 200, 201, 599, 600], [0, 200, 400, 600]),  # one-element pieces at the edges
+]
+
+
+@pytest.mark.parametrize(("cu", "bounds"), SLAB_CONTRACT_CASES)
+@pytest.mark.parametrize("r2l", [False, True])
+def test_seeded_slab_contract_in_fp64(cu, bounds, r2l):
+  """The row I/O contract of ascan_forward_slab / ascan_backward_slab restated
+  with the oracle on each slab alone: the row carry folded into the row's
+  first element in scan order (forward x' = x + g Y and g' = g A; backward an
+  additive adjoint term), the state halo as the edge element's neighbour, and
+  the row aggregate (``_slab_agg_reference``) reproduce the oracle of the
+  whole axis, with the carries and halos read off that oracle as the GPU test
+  of the seeded passes reads them."""
+  C, L = 3, bounds[-1]
+  rng = np.random.default_rng(len(cu))
+  g = (1 - (rng.random((C, L)) < 0.1) / 256).astype(np.float32)
+  x = rng.standard_normal((C, L)).astype(np.float32)
+  dy = rng.standard_normal((C, L)).astype(np.float32)
+  starts = set(cu)
+  y, A = oracle.scan_fwd(g, x, cu, reverse=r2l)
+  h = y.astype(np.float32)
+  dx, dg = oracle.scan_bwd(dy, g, h, cu, causal=not r2l)
+  tol = dict(rtol=1e-5, atol=1e-5)
+  for p in ts.plan_slabs(cu, bounds):
+    a, b = p.t0, p.t1
+    n, lcu = b - a, list(p.local_cu)
+    gs, xs, dys = (t[:, a:b].astype(np.float64) for t in (g, x, dy))
+    # forward: the carry enters at column n-1 (reverse) or 0
+    src = b if r2l else a - 1
+    if 0 <= src < L and (b if r2l else a) not in starts:
+      carry = np.stack([A[:, src], y[:, src]], 1)
+    else:
+      carry = np.stack([np.ones(C), np.zeros(C)], 1)
+    first = n - 1 if r2l else 0
+    gs2, xs2 = gs.copy(), xs.copy()
+    xs2[:, first] += gs[:, first] * carry[:, 1]
+    gs2[:, first] *= carry[:, 0]
+    ys, As = oracle.scan_fwd(gs2, xs2, lcu, reverse=r2l)
+    np.testing.assert_allclose(ys, y[:, a:b], **tol, err_msg=f"forward slab {a}")
+    np.testing.assert_allclose(As, A[:, a:b], **tol, err_msg=f"gate products slab {a}")
+    last = 0 if r2l else n - 1
+    agg = _slab_agg_reference(gs, xs, lcu, True, r2l, carry)
+    np.testing.assert_allclose(agg, np.stack([A[:, a + last], y[:, a + last]], 1), **tol,
+                               err_msg=f"forward aggregate slab {a}")
+    # backward: the adjoint term from column b (causal) or a - 1, the state
+    # neighbour from column a - 1 (causal) or b
+    nb = a - 1 if r2l else b
+    linked = 0 <= nb < L and (a if r2l else b) not in starts
+    bcarry = g[:, nb].astype(np.float64) * dx[:, nb] if linked else np.zeros(C)
+    hn = b if r2l else a - 1
+    halo = h[:, hn].astype(np.float64) if 0 <= hn < L and (b if r2l else a) not in starts \
+        else np.zeros(C)
+    dys2 = dys.copy()
+    dys2[:, 0 if r2l else n - 1] += bcarry
+    dxs, dgs = oracle.scan_bwd(dys2, g[:, a:b], h[:, a:b], lcu, causal=not r2l)
+    edge = n - 1 if r2l else 0  # the element whose state neighbour is the halo
+    dgs[:, edge] = dxs[:, edge] * halo
+    np.testing.assert_allclose(dxs, dx[:, a:b], **tol, err_msg=f"d_tokens slab {a}")
+    np.testing.assert_allclose(dgs, dg[:, a:b], **tol, err_msg=f"d_gates slab {a}")
+    bagg = _slab_agg_reference(gs, dys, lcu, False, not r2l, bcarry)
+    np.testing.assert_allclose(bagg[:, 1], dx[:, a + (n - 1 if r2l else 0)], **tol,
+                               err_msg=f"backward aggregate slab {a}")
+
+
 # --- GPU: emulated slabs against the oracle on the whole axis ---------------------------
 
 CASES = [
