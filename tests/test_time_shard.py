@@ -595,6 +595,9 @@ SEEDED_CASES = [
   (8, 49152, [0, 49152], [0, 16384, 32768, 49152]),
   # equal sequences of whole tiles in every slab: segment order
   (8, 49152, list(range(0, 49153, 8192)), [0, 16384, 32768, 49152]),
+  # the middle slab splits into two equal pieces that both continue from the
+  # neighbouring slabs: segment order with carries in both directions
+  (8, 49152, [0, 24576, 49152], [0, 16384, 32768, 49152]),
   # a sequence start at a slab edge and one inside a slab
   (8, 49152, [0, 16384, 20000, 49152], [0, 16384, 32768, 49152]),
   # rows that are not whole tiles: the slab kernels (row I/O in the consumers)
