@@ -291,21 +291,43 @@ class PeerExchange:
   @classmethod
   def connect(cls, num_channels: int, device, group=None) -> "PeerExchange":
     """Every rank of ``group`` creates its buffer; the IPC handles go round
-    with one ``all_gather_object`` and every rank maps the others' buffers."""
+    with one ``all_gather_object`` and every rank maps the others' buffers.
+
+    When a step fails, the error propagates after this rank has unmapped the
+    buffers it already mapped; its own buffer is freed only if its handle
+    never left the process (once the handles went round, another rank may
+    hold a mapping of it, and it stays allocated until the process ends)."""
     import torch.distributed as dist
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     device = torch.device(device)
     own = _lib.exchange_create(num_channels, device)
-    handles: list = [None] * world
-    dist.all_gather_object(handles, _lib.exchange_export(own), group=group)
-    addresses, mapped = [], []
-    for j, h in enumerate(handles):
-      if j == rank:
-        addresses.append(own)
-      else:
-        peer = _lib.exchange_import(h, device)
-        mapped.append(peer)
-        addresses.append(peer)
+    shared = False
+    mapped: list[int] = []
+    try:
+      handle = _lib.exchange_export(own)
+      handles: list = [None] * world
+      shared = True  # from here on, other ranks may map the buffer
+      dist.all_gather_object(handles, handle, group=group)
+      addresses = []
+      for j, h in enumerate(handles):
+        if j == rank:
+          addresses.append(own)
+        else:
+          peer = _lib.exchange_import(h, device)
+          mapped.append(peer)
+          addresses.append(peer)
+    except BaseException:
+      for peer in mapped:
+        try:
+          _lib.exchange_close(peer)
+        except Exception:  # keep the original error
+          pass
+      if not shared:
+        try:
+          _lib.exchange_destroy(own)
+        except Exception:
+          pass
+      raise
     return cls(num_channels, world, rank, device, own, addresses, mapped)
 
   @classmethod

@@ -224,6 +224,91 @@ def test_seeded_slab_contract_in_fp64(cu, bounds, r2l):
                                err_msg=f"backward aggregate slab {a}")
 
 
+def _connect_worker(rank, world, port, fail, outq):
+  """PeerExchange.connect on gloo with the library's buffer calls replaced by
+  fakes that log what they do; ``fail``: "import" (the last rank cannot map
+  the last peer's buffer) or "export" (one rank cannot export its handle)."""
+  import torch.distributed as dist
+  from associative_scan_triton import _lib
+  try:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    calls, own = [], 0x1000 * (rank + 1)
+
+    def create(C, device):
+      calls.append(("create", own))
+      return own
+
+    def export(buf):
+      if fail == "export":
+        raise _lib.ScanError("fake export failure")
+      return bytes([rank]) * _lib.IPC_HANDLE_BYTES
+
+    def import_(h, device):
+      src = h[0]
+      if fail == "import" and rank == world - 1 and src == world - 2:
+        raise _lib.ScanError("fake import failure")
+      calls.append(("import", src))
+      return 0x100000 + src
+
+    _lib.exchange_create, _lib.exchange_export, _lib.exchange_import = create, export, import_
+    _lib.exchange_close = lambda p: calls.append(("close", p))
+    _lib.exchange_destroy = lambda b: calls.append(("destroy", b))
+    try:
+      ex = ts.PeerExchange.connect(4, "cpu")
+      outq.put((rank, "ok", ex.table.tolist(), ex.mapped, calls))
+    except _lib.ScanError:
+      outq.put((rank, "failed", None, None, calls))
+    dist.destroy_process_group()
+  except BaseException as e:  # reported to the parent
+    outq.put((rank, f"error {type(e).__name__}: {e}", None, None, None))
+    raise
+
+
+def _run_connect(world, fail):
+  import multiprocessing as mp
+  ctx = mp.get_context("spawn")
+  outq = ctx.Queue()
+  port = _free_port()
+  procs = [ctx.Process(target=_connect_worker, args=(r, world, port, fail, outq))
+           for r in range(world)]
+  for p in procs:
+    p.start()
+  for p in procs:
+    p.join(timeout=120)
+  for p in procs:
+    if p.is_alive():
+      p.kill()
+  got = {}
+  while not outq.empty():
+    r, *rest = outq.get()
+    got[r] = rest
+  assert sorted(got) == list(range(world)), got
+  return got
+
+
+def test_peer_exchange_connect_on_gloo_ranks():
+  """Host side of PeerExchange.connect: every rank's table holds its own
+  buffer and the other ranks' mapped buffers; a rank that fails to map a
+  peer unmaps what it had mapped and keeps its own buffer (the handles went
+  round); a rank whose export fails frees its buffer (nobody saw it)."""
+  world = 3
+  got = _run_connect(world, "none")
+  for r in range(world):
+    status, table, mapped, _ = got[r]
+    assert status == "ok"
+    assert table == [0x1000 * (r + 1) if j == r else 0x100000 + j for j in range(world)]
+    assert mapped == [0x100000 + j for j in range(world) if j != r]
+  got = _run_connect(world, "import")
+  status, _, _, calls = got[world - 1]
+  assert status == "failed"
+  assert ("close", 0x100000) in calls and not any(c[0] == "destroy" for c in calls)
+  assert all(got[r][0] == "ok" for r in range(world - 1))
+  got = _run_connect(1, "export")
+  status, _, _, calls = got[0]
+  assert status == "failed" and ("destroy", 0x1000) in calls
+
+
 # --- GPU: emulated slabs against the oracle on the whole axis ---------------------------
 
 CASES = [
